@@ -1,0 +1,370 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 fused FP8 block-scale DeepSeek-V3 MoE layer.
+
+One "step" is one layer call ``kernel(...)`` over one batch of T tokens with
+the definition's shapes (H=7168, I=2048, 256 experts, top-8, 32 local
+experts).  Inputs are seeded synthetic tensors (the contest workload dataset
+is not available): weights ~N(0,1)/sqrt(K) quantised per 128x128 block,
+hidden ~N(0,1) quantised per 1x128, logits ~N(0,1).
+
+Default (N=1): the decode configuration T=64 (the largest
+decode batch) is the headline; T=1, 16 (decode) and 1024, 4096 (prefill,
+config 2) are reported in ``sweep``.  L2 is flushed (a 256 MiB write) before
+every timed step, outside the step's events.
+
+``--impl reference`` times the reference's CPU implementation of the layer
+(the oracle port of ``solution/cuda/moe.cu:137-240`` on the host cores).
+
+Prints ONE JSON line on rank 0.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+import __graft_entry__ as graft  # noqa: E402
+
+H, I = 7168, 2048
+W13_BYTES, W2_BYTES = 2 * I * H, H * I                 # per expert
+W13_SCALE_BYTES, W2_SCALE_BYTES = 32 * 56 * 4, 56 * 16 * 4
+TOKEN_BYTES = 256 * 4 + H + 56 * 4 + H * 2             # logits + hidden + scales + bf16 output
+FLOPS_PER_ASSIGNMENT = 2 * H * 2 * I + 2 * I * H
+FLUSH_BYTES = 256 << 20
+STAGES = ("route", "scan", "permute", "gemm1", "gemm2", "combine")
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--tokens", type=int, default=64, help="headline T")
+    p.add_argument("--sweep", default="1,16,1024,4096", help="extra T values ('' for none)")
+    p.add_argument("--local-experts", type=int, default=32)
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--cpu-sample-s", type=float, default=12.0)
+    return p.parse_args()
+
+
+def measured_peaks():
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling (200 ms) while the timed region runs."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.file.flush()
+        rows = [r.split(",") for r in pathlib.Path(self.file.name).read_text().splitlines() if r.strip()]
+        os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ---------------------------------------------------------------------------- workload
+def token_slice(base, T):
+    """Token-side inputs for T tokens cut from a larger seeded batch; weights shared."""
+    d = dict(base)
+    d["routing_logits"] = base["routing_logits"][:T].contiguous()
+    d["hidden_states"] = base["hidden_states"][:T].contiguous()
+    d["hidden_states_scale"] = base["hidden_states_scale"][:, :T].contiguous()
+    return d
+
+
+def routing_stats(K, L, inp, T, E_l):
+    """(active local experts, local assignments) of this batch, read from the workspace."""
+    lay = K.workspace_layout(T, E_l)
+    ws = K._workspaces[torch.cuda.current_device()]
+    seg = ws[lay.seg_offsets:lay.seg_offsets + 4 * (E_l + 1)].view(torch.int32).cpu()
+    counts = seg[1:] - seg[:-1]
+    return int((counts > 0).sum()), int(seg[-1])
+
+
+def algorithmic_bytes(T, n_act, R):
+    g1 = n_act * (W13_BYTES + W13_SCALE_BYTES) + R * (H + 56 * 4) + R * (2 * I + 16 * 4)
+    g2 = n_act * (W2_BYTES + W2_SCALE_BYTES) + R * (2 * I + 16 * 4) + R * H * 4
+    layer = n_act * (W13_BYTES + W2_BYTES + W13_SCALE_BYTES + W2_SCALE_BYTES) + T * TOKEN_BYTES
+    return {"gemm1": g1, "gemm2": g2, "layer": layer}
+
+
+def time_steps(fn, steps, warmup, flush):
+    """Per-step CUDA-event timing on the current stream, L2 flushed before each step."""
+    for _ in range(warmup):
+        flush.fill_(1)
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        evs[i][0].record()
+        fn()
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def stage_times(L, fn, steps, flush):
+    """Per-kernel durations from events the library records between its launches."""
+    lib = L.load()
+    per = {s: [] for s in STAGES}
+    for _ in range(steps):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
+        arr = (ctypes.c_void_p * 7)(*[ctypes.c_void_p(e.cuda_event) for e in evs])
+        for e in evs:          # materialise the events on this device
+            e.record()
+        flush.fill_(3)
+        torch.cuda.synchronize()
+        L.check(lib.moe_fp8_ds_set_stage_events(arr, 7), "set_stage_events")
+        fn()
+        L.check(lib.moe_fp8_ds_set_stage_events(None, 0), "set_stage_events")
+        torch.cuda.synchronize()
+        for i, s in enumerate(STAGES):
+            per[s].append(evs[i].elapsed_time(evs[i + 1]))
+    return {s: statistics.mean(v) for s, v in per.items()}
+
+
+def e2e_steps(pkg, inp, T, steps, warmup):
+    """Public kernel(...) with the step's activations copied from pinned host memory
+    and the bf16 output read back, all inside the timed region (weights resident)."""
+    dev = inp["hidden_states"].device
+    h_logits = inp["routing_logits"].cpu().pin_memory()
+    h_hidden = inp["hidden_states"].view(torch.uint8).cpu().pin_memory()
+    h_scale = inp["hidden_states_scale"].cpu().pin_memory()
+    h_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    d_logits = torch.empty_like(inp["routing_logits"])
+    d_hidden = torch.empty(T, H, dtype=torch.uint8, device=dev)
+    d_scale = torch.empty_like(inp["hidden_states_scale"])
+    d_out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        d_logits.copy_(h_logits, non_blocking=True)
+        d_hidden.copy_(h_hidden, non_blocking=True)
+        d_scale.copy_(h_scale, non_blocking=True)
+        pkg.kernel(d_logits, inp["routing_bias"], d_hidden.view(torch.float8_e4m3fn), d_scale,
+                   inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"],
+                   inp["gemm2_weights_scale"], inp["local_expert_offset"], inp["routed_scaling_factor"], d_out)
+        h_out.copy_(d_out, non_blocking=True)
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / steps
+    h2d = h_logits.numel() * 4 + h_hidden.numel() + h_scale.numel() * 4
+    return ms, h2d, h_out.numel() * 2
+
+
+def cpu_baseline(inp_dev, sample_s):
+    from oracle import moe_ref
+    cpu = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp_dev.items()}
+    torch.set_num_threads(os.cpu_count() or 1)
+    args = graft.load_package().inputs.as_args(cpu)
+    times = []
+    t_start = time.perf_counter()
+    while not times or (time.perf_counter() - t_start < sample_s and len(times) < 5):
+        t0 = time.perf_counter()
+        moe_ref.moe_forward(*args)
+        times.append(time.perf_counter() - t0)
+    return statistics.mean(times), len(times), torch.get_num_threads()
+
+
+def traffic_from_profile(workload, kernel):
+    f = ROOT / "profiles" / "dram_traffic.json"
+    if not f.exists():
+        return None
+    d = json.loads(f.read_text())
+    return d.get(workload, {}).get(kernel)
+
+
+# ---------------------------------------------------------------------------- arms
+def run_reference_arm(a, T, E_l):
+    from oracle import moe_ref
+    pkg = graft.load_package()
+    torch.set_num_threads(os.cpu_count() or 1)
+    inp = pkg.inputs.make_inputs(T, E_l=E_l, seed=0)
+    args = pkg.inputs.as_args(inp)
+    for _ in range(a.warmup):
+        moe_ref.moe_forward(*args)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        moe_ref.moe_forward(*args)
+    dt = (time.perf_counter() - t0) / a.steps
+    v = T / dt
+    line = {
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s",
+        "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic",
+        "config": {"workload": f"decode_T{T}_E{E_l}", "tokens": T, "local_experts": E_l,
+                   "note": "reference CPU path (oracle port of solution/cuda/moe.cu:137-240, fp32 on host cores)"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{a.steps} full layer calls at T={T}, E_l={E_l}"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    a = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    E_l = a.local_experts
+    T = a.tokens
+
+    if a.impl == "reference":
+        if rank == 0:
+            run_reference_arm(a, T, E_l)
+        return
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    pkg = graft.load_package()
+    K = sys.modules["fib_b200.kernel"]
+    L = sys.modules["fib_b200._lib"]
+    hbm_peak, peak_kind = measured_peaks()
+
+    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep else []
+    T_max = max([T] + sweep_T)
+    # Each rank holds the 32 experts of one expert-parallel slot (offset 32*rank).
+    offset = (E_l * rank) % 256
+    base = pkg.inputs.make_inputs(T_max, E_l=E_l, local_expert_offset=offset, seed=rank, device=dev)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def measure(Tm, steps, warmup):
+        inp = token_slice(base, Tm)
+        out = torch.empty(Tm, H, dtype=torch.bfloat16, device=dev)
+        fn = lambda: pkg.kernel(*pkg.inputs.as_args(inp), out)  # noqa: E731
+        ts = time_steps(fn, steps, warmup, flush)
+        n_act, R = routing_stats(K, L, inp, Tm, E_l)
+        return inp, fn, ts, n_act, R
+
+    # ---- headline
+    inp, fn, ts, n_act, R = measure(T, a.warmup, a.warmup)     # warm everything once
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ts = time_steps(fn, a.steps, a.warmup, flush)
+    clocks = clk.summary()
+    ms = sum(ts) / len(ts)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t)
+    value = T * world / (ms * 1e-3)
+    stages = stage_times(L, fn, max(3, min(a.steps, 10)), flush)
+    ab = algorithmic_bytes(T, n_act, R)
+    dom = max(("gemm1", "gemm2"), key=lambda s: stages[s])
+    achieved = ab[dom] / (stages[dom] * 1e-3) / 1e9
+    e2e_ms, h2d, d2h = e2e_steps(pkg, inp, T, a.steps, a.warmup)
+
+    sweep = []
+    for Ts in sweep_T:
+        _, _, tss, na, Rs = measure(Ts, a.steps, a.warmup)
+        mss = sum(tss) / len(tss)
+        bb = algorithmic_bytes(Ts, na, Rs)["layer"]
+        sweep.append({"tokens": Ts, "us_per_call": mss * 1e3, "tokens_per_s": Ts / (mss * 1e-3),
+                      "active_experts": na, "assignments": Rs, "hbm_gbs": bb / (mss * 1e-3) / 1e9,
+                      "hbm_frac": bb / (mss * 1e-3) / 1e9 / hbm_peak,
+                      "fp8_tflops": Rs * FLOPS_PER_ASSIGNMENT / (mss * 1e-3) / 1e12})
+
+    cpu = None
+    if rank == 0 and not a.no_cpu_baseline:
+        sec, n, cores = cpu_baseline(inp, a.cpu_sample_s)
+        cpu = {"value": T / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
+               "sample": f"{n} full layer call(s) at T={T}, E_l={E_l} (fp32 oracle port, {sec:.2f} s/call)"}
+
+    workload = f"decode_T{T}_E{E_l}"
+    line = {
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp8e4m3 (fp32 accumulate)", "data": "synthetic",
+        "config": {"workload": workload, "tokens": T, "local_experts": E_l, "hidden": H, "intermediate": I,
+                   "experts": 256, "top_k": 8, "parallelism": "replicas" if world > 1 else "single",
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "active_experts": n_act, "assignments": R,
+                   "layer_hbm_gbs": ab["layer"] / (ms * 1e-3) / 1e9,
+                   "layer_hbm_frac": ab["layer"] / (ms * 1e-3) / 1e9 / hbm_peak,
+                   "us_per_call": ms * 1e3},
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                     "algorithmic_bytes": ab[dom], "kernel_ms": stages[dom],
+                     "traffic": traffic_from_profile(workload, dom)},
+        "stage_ms": stages,
+        "sweep": sweep,
+        "cpu_baseline": cpu,
+        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "clocks": clocks,
+        "gpu_launches": a.steps * L.load().moe_fp8_ds_launches_per_call(),
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,342 @@
+// C ABI and host orchestration of the fused FP8 DeepSeek-V3 MoE layer.
+//
+// Replaces the host pipeline run(...) of the reference
+// (solution/python/main.cpp:66-266): the same six steps (route, count/scan,
+// permute+gather, GEMM1+SwiGLU, GEMM2, combine) as six kernel launches on the
+// caller's stream, with every intermediate carved out of one caller-owned
+// workspace instead of ~25 per-call torch allocations, and no host sync.
+#include <mutex>
+#include <string.h>
+
+#include "kernels.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool init = false;
+  int sm_count = 0;
+  int major = 0;
+};
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_mu;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+int g_bn_override[2] = {0, 0};
+cudaEvent_t g_stage_events[7] = {};
+bool g_stage_events_on = false;
+
+void mark_stage(int i, cudaStream_t s) {
+  if (g_stage_events_on) cudaEventRecord(g_stage_events[i], s);
+}
+
+int device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MOE_ERR_NO_DEVICE;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.init) {
+    if (cudaDeviceGetAttribute(&d.sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      return MOE_ERR_NO_DEVICE;
+    if (cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+      return MOE_ERR_NO_DEVICE;
+    d.init = true;
+  }
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return MOE_ERR_NO_DEVICE;
+    g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+  }
+  *out = d;
+  return d.major == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
+}
+
+// Token-tile width per GEMM from the expected tokens per active expert.
+int pick_bn(int T, int E_l) {
+  const double per_expert = (double)T * kTopK / kExpertsGlobal;
+  (void)E_l;
+  if (per_expert <= 12.0) return 16;
+  if (per_expert <= 24.0) return 32;
+  if (per_expert <= 48.0) return 64;
+  return 128;
+}
+
+struct Plan {
+  moe_fp8_ds_layout pub;
+  int T, E_l, NB, R_cap, bn1, bn2, grid, max_mt1, max_mt2;
+  uint64_t hist, tiles1, tiles2, sched, counters1, counters2, partials1, partials2;
+};
+
+uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
+
+void make_plan(int T, int E_l, int sm_count, Plan* P) {
+  memset(P, 0, sizeof(*P));
+  P->T = T;
+  P->E_l = E_l;
+  P->NB = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+  P->R_cap = T * (E_l < kTopK ? E_l : kTopK);
+  P->bn1 = g_bn_override[0] ? g_bn_override[0] : pick_bn(T, E_l);
+  P->bn2 = g_bn_override[1] ? g_bn_override[1] : pick_bn(T, E_l);
+  P->grid = sm_count;
+  auto max_mt = [&](int bn) {
+    long v = (long)P->R_cap / bn + E_l;
+    return (int)(v < P->R_cap ? v : P->R_cap);
+  };
+  P->max_mt1 = max_mt(P->bn1);
+  P->max_mt2 = max_mt(P->bn2);
+  uint64_t off = 0;
+  auto take = [&](uint64_t bytes) { uint64_t o = off; off = align256(off + bytes); return o; };
+  const uint64_t R = (uint64_t)P->R_cap;
+  P->pub.error_word = take(16);
+  P->pub.topk_ids = take((uint64_t)T * kTopK * 4);
+  P->pub.topk_weights = take((uint64_t)T * kTopK * 4);
+  P->pub.inv_row = take((uint64_t)T * kTopK * 4);
+  P->hist = take((uint64_t)P->NB * E_l * 4);
+  P->pub.seg_offsets = take((uint64_t)(E_l + 1) * 4);
+  P->tiles1 = take((uint64_t)P->max_mt1 * 16);
+  P->tiles2 = take((uint64_t)P->max_mt2 * 16);
+  P->sched = take(64);
+  P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
+  P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
+  P->pub.row_token = take(R * 4);
+  P->pub.act = take(R * kHidden);
+  P->pub.act_scale = take(R * kHiddenBlocks * 4);
+  P->pub.inter = take(2 * R * kInter);
+  P->pub.inter_scale = take(R * kInterBlocks * 4);
+  P->pub.down = take(R * kHidden * 4);
+  P->partials1 = take(gemm_partials_bytes(1, P->bn1, P->grid));
+  P->partials2 = take(gemm_partials_bytes(2, P->bn2, P->grid));
+  P->pub.total_bytes = off;
+  P->pub.row_capacity = P->R_cap;
+}
+
+bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {inner};          // bytes (1-byte elements)
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+                        box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int validate_common(const moe_fp8_ds_args* a, bool routed) {
+  if (!a) return MOE_ERR_INVALID_ARGUMENT;
+  if (a->num_tokens < 0 || a->num_local_experts < 1 || a->num_local_experts > kExpertsGlobal)
+    return MOE_ERR_INVALID_ARGUMENT;
+  if (a->num_tokens > (1 << 20)) return MOE_ERR_TOO_LARGE;
+  if (a->num_tokens == 0) return MOE_OK;
+  const void* need[] = {a->hidden_states, a->hidden_states_scale, a->gemm1_weights,
+                        a->gemm1_weights_scale, a->gemm2_weights, a->gemm2_weights_scale};
+  for (const void* p : need) if (!p) return MOE_ERR_INVALID_ARGUMENT;
+  if (!a->output && !a->output_f32) return MOE_ERR_INVALID_ARGUMENT;
+  if (routed) {
+    if (!a->topk_ids || !a->topk_weights) return MOE_ERR_INVALID_ARGUMENT;
+  } else {
+    if (!a->routing_logits || !a->routing_bias) return MOE_ERR_INVALID_ARGUMENT;
+    if (!aligned16(a->routing_logits) || !aligned16(a->routing_bias)) return MOE_ERR_MISALIGNED;
+  }
+  if (!aligned16(a->hidden_states) || !aligned16(a->gemm1_weights) || !aligned16(a->gemm2_weights) ||
+      !aligned16(a->output ? a->output : a->output_f32))
+    return MOE_ERR_MISALIGNED;
+  return MOE_OK;
+}
+
+int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream, bool routed) {
+  int st = validate_common(a, routed);
+  if (st != MOE_OK) return st;
+  const int T = a->num_tokens, E_l = a->num_local_experts;
+  if (T == 0) return MOE_OK;
+  DeviceInfo dev;
+  st = device_info(&dev);
+  if (st != MOE_OK) return st;
+  Plan P;
+  make_plan(T, E_l, dev.sm_count, &P);
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255)) return MOE_ERR_MISALIGNED;
+  if (ws_bytes < P.pub.total_bytes) return MOE_ERR_WORKSPACE_TOO_SMALL;
+  uint8_t* base = static_cast<uint8_t*>(ws);
+  auto at = [&](uint64_t off) { return base + off; };
+  int* err = reinterpret_cast<int*>(at(P.pub.error_word));
+  int32_t* ids = routed ? const_cast<int32_t*>(a->topk_ids) : reinterpret_cast<int32_t*>(at(P.pub.topk_ids));
+  float* wts = routed ? const_cast<float*>(a->topk_weights) : reinterpret_cast<float*>(at(P.pub.topk_weights));
+  int32_t* inv = reinterpret_cast<int32_t*>(at(P.pub.inv_row));
+  int32_t* hist = reinterpret_cast<int32_t*>(at(P.hist));
+  int32_t* seg = reinterpret_cast<int32_t*>(at(P.pub.seg_offsets));
+  int4* tiles1 = reinterpret_cast<int4*>(at(P.tiles1));
+  int4* tiles2 = reinterpret_cast<int4*>(at(P.tiles2));
+  int32_t* sched = reinterpret_cast<int32_t*>(at(P.sched));
+  int32_t* cnt1 = reinterpret_cast<int32_t*>(at(P.counters1));
+  int32_t* cnt2 = reinterpret_cast<int32_t*>(at(P.counters2));
+  int32_t* row_token = reinterpret_cast<int32_t*>(at(P.pub.row_token));
+  uint8_t* act = at(P.pub.act);
+  float* act_scale = reinterpret_cast<float*>(at(P.pub.act_scale));
+  uint8_t* inter = at(P.pub.inter);
+  float* inter_scale = reinterpret_cast<float*>(at(P.pub.inter_scale));
+  float* down = reinterpret_cast<float*>(at(P.pub.down));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
+  if (!encode_2d(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128) ||
+      !encode_2d(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
+      !encode_2d(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128) ||
+      !encode_2d(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2)))
+    return MOE_ERR_INVALID_ARGUMENT;
+
+  cudaError_t ce;
+  mark_stage(0, s);
+  ce = launch_route_hist(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
+                         a->local_expert_offset, E_l, ids, wts, hist, err, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  mark_stage(1, s);
+  ce = launch_scan(hist, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1, kInter / 128,
+                   cnt2, kHidden / 128, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  mark_stage(2, s);
+  ce = launch_scatter_gather(ids, hist, T, E_l, a->local_expert_offset, P.R_cap, a->hidden_states,
+                             a->hidden_states_scale, inv, row_token, act, act_scale, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+
+  GemmParams g1{};
+  g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale; g1.b_scale = act_scale;
+  g1.counters = cnt1; g1.partials = reinterpret_cast<float*>(at(P.partials1));
+  g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
+  mark_stage(3, s);
+  ce = launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+
+  GemmParams g2{};
+  g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale; g2.b_scale = inter_scale;
+  g2.counters = cnt2; g2.partials = reinterpret_cast<float*>(at(P.partials2));
+  g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
+  mark_stage(4, s);
+  ce = launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+
+  mark_stage(5, s);
+  ce = launch_combine(down, inv, wts, T, a->output, a->output_f32, s);
+  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  mark_stage(6, s);
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+int moe_fp8_ds_workspace_layout(int32_t num_tokens, int32_t num_local_experts,
+                                moe_fp8_ds_layout* layout) {
+  if (!layout || num_tokens < 0 || num_local_experts < 1 || num_local_experts > kExpertsGlobal)
+    return MOE_ERR_INVALID_ARGUMENT;
+  if (num_tokens > (1 << 20)) return MOE_ERR_TOO_LARGE;
+  DeviceInfo dev;
+  int st = device_info(&dev);
+  if (st != MOE_OK) return st;
+  Plan P;
+  make_plan(num_tokens, num_local_experts, dev.sm_count, &P);
+  *layout = P.pub;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_workspace_size(int32_t num_tokens, int32_t num_local_experts, uint64_t* bytes) {
+  if (!bytes) return MOE_ERR_INVALID_ARGUMENT;
+  moe_fp8_ds_layout l;
+  int st = moe_fp8_ds_workspace_layout(num_tokens, num_local_experts, &l);
+  if (st != MOE_OK) return st;
+  *bytes = l.total_bytes;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_run(const moe_fp8_ds_args* args, void* workspace, uint64_t workspace_bytes,
+                   void* stream) {
+  return run_impl(args, workspace, workspace_bytes, stream, false);
+}
+
+int moe_fp8_ds_run_routed(const moe_fp8_ds_args* args, void* workspace, uint64_t workspace_bytes,
+                          void* stream) {
+  return run_impl(args, workspace, workspace_bytes, stream, true);
+}
+
+int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
+                     float routed_scaling_factor, int32_t* topk_ids, float* topk_weights,
+                     void* stream) {
+  if (num_tokens < 0 || (num_tokens > 0 && (!routing_logits || !routing_bias || !topk_ids || !topk_weights)))
+    return MOE_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MOE_OK;
+  DeviceInfo dev;
+  int st = device_info(&dev);
+  if (st != MOE_OK) return st;
+  // No local experts (E_l = 0, no histogram): routing only.
+  cudaError_t ce = launch_route_hist(false, routing_logits, routing_bias, num_tokens,
+                                     routed_scaling_factor, 0, 0, topk_ids, topk_weights,
+                                     nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  return ce == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t* device_error) {
+  if (!workspace || !device_error) return MOE_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  if (cudaMemcpyAsync(&v, workspace, 4, cudaMemcpyDeviceToHost, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (cudaMemsetAsync(workspace, 0, 16, s) != cudaSuccess) return MOE_ERR_CUDA;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return MOE_ERR_CUDA;
+  *device_error = v;
+  if (v == kDevOk) return MOE_OK;
+  if (v == kDevTimeoutProducer || v == kDevTimeoutMma || v == kDevTimeoutEpilogue)
+    return MOE_ERR_DEVICE_TIMEOUT;
+  return MOE_ERR_DEVICE_FAULT;
+}
+
+const char* moe_fp8_ds_status_string(int status) {
+  switch (status) {
+    case MOE_OK: return "ok";
+    case MOE_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MOE_ERR_MISALIGNED: return "pointer not 16-byte aligned (workspace: 256-byte)";
+    case MOE_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case MOE_ERR_CUDA: return "CUDA runtime error";
+    case MOE_ERR_NO_DEVICE: return "no sm_100 device or driver entry point";
+    case MOE_ERR_DEVICE_TIMEOUT: return "device-side wait timed out";
+    case MOE_ERR_DEVICE_FAULT: return "device-side check failed";
+    case MOE_ERR_TOO_LARGE: return "size exceeds the entry point's limit";
+  }
+  return "unknown status";
+}
+
+int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2) {
+  auto ok = [](int v) { return v == 0 || v == 16 || v == 32 || v == 64 || v == 128; };
+  if (!ok(bn_gemm1) || !ok(bn_gemm2)) return MOE_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_bn_override[0] = bn_gemm1;
+  g_bn_override[1] = bn_gemm2;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (count == 0) { g_stage_events_on = false; return MOE_OK; }
+  if (count != 7 || !events) return MOE_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < 7; ++i) {
+    if (!events[i]) return MOE_ERR_INVALID_ARGUMENT;
+    g_stage_events[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  g_stage_events_on = true;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_launches_per_call(void) { return 6; }
+
+}  // extern "C"

@@ -1,0 +1,437 @@
+// Grouped FP8 block-scaled GEMMs of the MoE layer on the sm_100a tensor cores.
+//
+// Replaces the reference's CUTLASS grouped GEMMs
+// (solution/python/moe_grouped_gemm_fp8.cu:821-948 and 956-1075) and its
+// separate SwiGLU + requantisation kernel (solution/python/kernel.cu:1086-1145).
+//
+// Formulation ("swap AB"): the MMA's M=128 side is 128 weight rows, its N side
+// is a tile of BN tokens, so a decode step with one token per expert still
+// fills the tensor core's M dimension and the weight stream is the only large
+// operand.  Both operands are K-major e4m3 tiles loaded by TMA with 128-byte
+// swizzling; one tcgen05.mma of K=32 is issued four times per 128-wide K block.
+//
+// Block scales: the fp32 128x128 weight scale is a scalar per (tile, K block),
+// the fp32 1x128 activation scale is per token column.  Because they are
+// arbitrary fp32 values, each K block is accumulated into a fresh TMEM
+// partial that the epilogue warps read (tcgen05.ld) and add into registers as
+//     acc[j] += partial[j] * (w_scale * act_scale[j]).
+// TMEM partials are double buffered so the MMA of block k+1 overlaps the
+// promotion of block k.
+//
+// KIND 1 (GEMM1, 7168 -> 2x2048): each tile holds the X1 rows n..n+127 and the
+// X2 rows 2048+n..2048+n+127 of W13, so SwiGLU c = silu(X2)*X1 and the 1x128
+// requantisation of c are done in the epilogue.  c is stored as two e4m3
+// terms, c ~= hi*s + lo*(s/16) with s = amax/448, written as the row pair
+// (2r, 2r+1) of the intermediate.
+// KIND 2 (GEMM2, 2048 -> 7168): the token operand holds the hi and lo rows of
+// each token, so one MMA of N = 2*BN yields both; the epilogue folds them as
+// (P_hi + P_lo/16) * s.
+//
+// Scheduling: persistent, one CTA per SM, stream-K.  The work is the list of
+// (n-tile, token tile) units times K blocks; every CTA gets one contiguous
+// range of that iteration space.  A unit split between CTAs is finished by the
+// last contributor, which sums the partial tiles in fixed CTA order (so the
+// result is deterministic) and runs the epilogue.
+//
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer,
+// warps 2.. = epilogue (one or two warpgroups, split by token columns).
+#include "kernels.cuh"
+
+namespace moe {
+
+template <int KIND, int BN, int STAGES, int NWG>
+struct GemmCfg {
+  static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles per stage
+  static constexpr int MMA_N = KIND == 1 ? BN : 2 * BN;     // token-operand rows
+  static constexpr int KB = KIND == 1 ? kHiddenBlocks : kInterBlocks;
+  static constexpr int NT = KIND == 1 ? kInter / 128 : kHidden / 128;   // n-tiles per expert
+  static constexpr int W_ROWS = KIND == 1 ? kGemm1Out : kHidden;        // weight rows per expert
+  static constexpr int W_TILE = 128 * 128;
+  static constexpr int B_TILE = MMA_N * 128;
+  static constexpr int STAGE = NW * W_TILE + B_TILE;
+  static constexpr int TMEM_USED = 2 * NW * MMA_N;
+  static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64
+                                 : TMEM_USED <= 128 ? 128 : TMEM_USED <= 256 ? 256 : 512;
+  static constexpr int NEPI = 128 * NWG;
+  static constexpr int THREADS = 64 + NEPI;
+  static constexpr int CPW = BN / NWG;                      // token columns per warpgroup
+  static constexpr int AUX = 2048 + 2 * BN * 4 + NWG * 4 * CPW * 4;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
+  static_assert(TMEM_USED <= 512, "TMEM budget");
+  static_assert(CPW % 16 == 0 || (KIND == 2 && CPW % 8 == 0), "column chunking");
+  static_assert(MMA_N % 16 == 0 && MMA_N <= 256, "MMA N");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+struct Schedule {
+  int n_mt, units, total, L, it0, it1;
+};
+
+__device__ __forceinline__ Schedule make_schedule(int n_mt, int NT, int KB) {
+  Schedule s;
+  s.n_mt = n_mt;
+  s.units = n_mt * NT;
+  s.total = s.units * KB;
+  s.L = (s.total + gridDim.x - 1) / gridDim.x;
+  s.it0 = min(s.total, (int)blockIdx.x * s.L);
+  s.it1 = min(s.total, s.it0 + s.L);
+  return s;
+}
+
+template <int KIND, int BN, int STAGES, int NWG>
+__global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG>::THREADS, 1)
+moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
+                const GemmParams p) {
+  using C = GemmCfg<KIND, BN, STAGES, NWG>;
+  extern __shared__ uint8_t smem_raw[];
+  // 1024-byte alignment for 128-byte-swizzled TMA tiles.
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* aux = smem + STAGES * C::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(aux);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = const_cast<int*>(abort_flag) + 1;     // [NWG]
+  float* sbuf = reinterpret_cast<float*>(aux + 2048);      // [2][BN] token-column scales
+  float* samax = sbuf + 2 * BN;                            // [NWG][4][CPW]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KB);
+  if (sch.it0 >= sch.it1) return;   // uniform: this CTA has no work
+  const int n_iter = sch.it1 - sch.it0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NWG * 4); }
+    mbar_init(drain, 1);
+    *const_cast<int*>(abort_flag) = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tm_w); tma_prefetch_desc(&tm_b); }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one_lane()) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_b = l2_policy_evict_last();
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int it = sch.it0 + i;
+        const int u = it / C::KB, kb = it % C::KB;
+        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+        const int4 tile = p.tiles[mt];
+        const int s = i % STAGES;
+        if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        uint8_t* st = smem + s * C::STAGE;
+        const int x = kb * 128;
+        const int wrow = tile.x * C::W_ROWS + nt * 128;
+        tma_load_2d(&tm_w, &full[s], st, x, wrow, pol_w);
+        if (KIND == 1) tma_load_2d(&tm_w, &full[s], st + C::W_TILE, x, wrow + kInter, pol_w);
+        tma_load_2d(&tm_b, &full[s], st + C::NW * C::W_TILE, x,
+                    KIND == 1 ? tile.y : 2 * tile.y, pol_b);
+        ++issued;
+      }
+      if (!ok) {
+        raise_error(p.err, kDevTimeoutProducer);
+        // Let copies already in flight land before the CTA exits.
+        for (int i = max(0, issued - STAGES); i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+                 globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_lane()) {
+      constexpr uint32_t idesc = make_idesc_f8(128, C::MMA_N);
+      const uint32_t smem_base = smem_u32(smem);
+      bool ok = true;
+      for (int i = 0; i < n_iter; ++i) {
+        const int s = i % STAGES, b = i & 1;
+        if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&tempty[b], ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = smem_base + s * C::STAGE;
+        const uint64_t bdesc = make_sdesc_sw128(st + C::NW * C::W_TILE);
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w) {
+          const uint64_t adesc = make_sdesc_sw128(st + w * C::W_TILE);
+          const uint32_t d = tmem_base + (uint32_t)(b * C::NW * C::MMA_N + w * C::MMA_N);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)   // 4 x K=32 per 128-byte K block; +32 B = +2 in addr>>4
+            tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+        }
+        tc_commit(&empty[s]);
+        tc_commit(&tfull[b]);
+      }
+      if (!ok) raise_error(p.err, kDevTimeoutMma);
+      // Wait for every MMA this thread issued before TMEM is released.
+      tc_commit(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 64;            // 0 .. NEPI-1
+    const int wg = et >> 7;                     // warpgroup -> token-column half
+    const int q = warp & 3;                     // TMEM lane quarter this warp may access
+    const int f = q * 32 + lane;                // weight row inside the 128-row tile
+    const int j0 = wg * C::CPW;                 // first token column of this warpgroup
+    const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+
+    float acc[C::NW][C::CPW];
+    int seg_kb0 = 0;
+    int4 tile = make_int4(0, 0, 0, 0);
+
+    auto scale_for = [&](int it, int j) -> float {
+      const int u = it / C::KB, kb = it % C::KB;
+      const int4 tl = p.tiles[u % sch.n_mt];
+      return j < tl.z ? __ldg(p.b_scale + (size_t)kb * p.R_cap + tl.y + j) : 0.f;
+    };
+    if (et < BN) sbuf[et] = scale_for(sch.it0, et);
+    named_bar_sync(1, C::NEPI);
+
+    for (int i = 0; i < n_iter; ++i) {
+      const int it = sch.it0 + i;
+      const int u = it / C::KB, kb = it % C::KB;
+      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      const int b = i & 1;
+      if (i == 0 || kb == 0) {
+        tile = p.tiles[mt];
+        seg_kb0 = kb;
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+          for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
+      }
+      const float pre = (i + 1 < n_iter && et < BN) ? scale_for(it + 1, et) : 0.f;
+      float wsc[C::NW];
+#pragma unroll
+      for (int w = 0; w < C::NW; ++w) {
+        const int nb = KIND == 1 ? nt + w * (kInter / 128) : nt;
+        wsc[w] = __ldg(p.w_scale + ((size_t)tile.x * (C::W_ROWS / 128) + nb) * C::KB + kb);
+      }
+      const bool got = mbar_wait_bounded(&tfull[b], (i >> 1) & 1, abort_flag);
+      if (got) {
+        tc_fence_after();
+        const float* sb = sbuf + b * BN;   // buffer index = i & 1
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w) {
+          const uint32_t col0 = (uint32_t)(b * C::NW * C::MMA_N + w * C::MMA_N);
+          if (KIND == 1) {
+#pragma unroll
+            for (int c = 0; c < C::CPW / 16; ++c) {
+              float v[16];
+              tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int x = 0; x < 16; ++x) {
+                const int jj = c * 16 + x;
+                acc[w][jj] = fmaf(v[x], wsc[w] * sb[j0 + jj], acc[w][jj]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < C::CPW / 8; ++c) {
+              float v[16];
+              tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int x = 0; x < 8; ++x) {
+                const int jj = c * 8 + x;
+                const float pv = fmaf(v[2 * x + 1], 0.0625f, v[2 * x]);
+                acc[w][jj] = fmaf(pv, wsc[w] * sb[j0 + jj], acc[w][jj]);
+              }
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
+      }
+      if (et < BN) sbuf[((i + 1) & 1) * BN + et] = pre;
+      named_bar_sync(1, C::NEPI);
+      if (*abort_flag) break;
+
+      const bool seg_last = (kb == C::KB - 1) || (it == sch.it1 - 1);
+      if (!seg_last) continue;
+
+      // ---------------- end of this CTA's share of unit u
+      if (!(seg_kb0 == 0 && kb == C::KB - 1)) {
+        // stream-K: publish the partial, the last contributor finishes the unit
+        const int first_unit = sch.it0 / C::KB;
+        const int slot = (u == first_unit) ? 0 : 1;
+        float* mine = p.partials + ((size_t)(blockIdx.x * 2 + slot) * C::NW) * BN * 128;
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+          for (int jj = 0; jj < C::CPW; ++jj)
+            __stcg(mine + ((size_t)w * BN + j0 + jj) * 128 + f, acc[w][jj]);
+        __threadfence();
+        named_bar_sync(1, C::NEPI);
+        const int c_lo = (u * C::KB) / sch.L;
+        const int c_hi = ((u + 1) * C::KB - 1) / sch.L;
+        if (et == 0) {
+          const int old = atomicAdd(p.counters + u, 1);
+          last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
+        }
+        named_bar_sync(1, C::NEPI);
+        if (!last_flag[0]) continue;
+        __threadfence();
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+          for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
+        for (int c = c_lo; c <= c_hi; ++c) {
+          const int cslot = (u == (c * sch.L) / C::KB) ? 0 : 1;
+          const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
+#pragma unroll
+          for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+            for (int jj = 0; jj < C::CPW; ++jj)
+              acc[w][jj] += __ldcg(src + ((size_t)w * BN + j0 + jj) * 128 + f);
+        }
+      }
+
+      if (KIND == 1) {
+        // SwiGLU: c = silu(X2) * X1, X1 = acc[0], X2 = acc[1]
+        float* my_amax = samax + (wg * 4 + q) * C::CPW;
+#pragma unroll
+        for (int jj = 0; jj < C::CPW; ++jj) {
+          const float x1 = acc[0][jj], x2 = acc[C::NW - 1][jj];
+          const float cv = __fmul_rn(__fdiv_rn(x2, __fadd_rn(1.0f, expf(-x2))), x1);
+          acc[0][jj] = cv;
+          float m = fabsf(cv);
+#pragma unroll
+          for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+          if (lane == 0) my_amax[jj] = m;
+        }
+        named_bar_sync(2 + wg, 128);
+#pragma unroll
+        for (int jj = 0; jj < C::CPW; ++jj) {
+          const float* am = samax + wg * 4 * C::CPW + jj;
+          const float amax = fmaxf(fmaxf(am[0], am[C::CPW]), fmaxf(am[2 * C::CPW], am[3 * C::CPW]));
+          const float s = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+          const float inv = __frcp_rn(s);
+          const float cv = acc[0][jj];
+          const uint8_t hi = f32_to_e4m3(__fmul_rn(cv, inv));
+          const float resid = __fsub_rn(cv, __fmul_rn(e4m3_to_f32(hi), s));
+          const uint8_t lo = f32_to_e4m3(__fmul_rn(resid, __fmul_rn(inv, 16.0f)));
+          const int j = j0 + jj;
+          if (j < tile.z) {
+            const size_t row = (size_t)(tile.y + j);
+            p.inter[(2 * row) * kInter + nt * 128 + f] = hi;
+            p.inter[(2 * row + 1) * kInter + nt * 128 + f] = lo;
+            if (f == 0) p.inter_scale[(size_t)nt * p.R_cap + row] = s;
+          }
+        }
+        named_bar_sync(2 + wg, 128);
+      } else {
+#pragma unroll
+        for (int jj = 0; jj < C::CPW; ++jj) {
+          const int j = j0 + jj;
+          if (j < tile.z)
+            p.down[(size_t)(tile.y + j) * kHidden + nt * 128 + f] = acc[0][jj];
+        }
+      }
+    }
+    if (*abort_flag) raise_error(p.err, kDevTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Host-side dispatch
+// --------------------------------------------------------------------------
+template <int KIND, int BN> struct Pick;
+template <> struct Pick<1, 16> { using C = GemmCfg<1, 16, 6, 1>; static constexpr int S = 6, W = 1; };
+template <> struct Pick<1, 32> { using C = GemmCfg<1, 32, 6, 1>; static constexpr int S = 6, W = 1; };
+template <> struct Pick<1, 64> { using C = GemmCfg<1, 64, 5, 1>; static constexpr int S = 5, W = 1; };
+template <> struct Pick<1, 128> { using C = GemmCfg<1, 128, 4, 2>; static constexpr int S = 4, W = 2; };
+template <> struct Pick<2, 16> { using C = GemmCfg<2, 16, 10, 1>; static constexpr int S = 10, W = 1; };
+template <> struct Pick<2, 32> { using C = GemmCfg<2, 32, 8, 1>; static constexpr int S = 8, W = 1; };
+template <> struct Pick<2, 64> { using C = GemmCfg<2, 64, 6, 1>; static constexpr int S = 6, W = 1; };
+template <> struct Pick<2, 128> { using C = GemmCfg<2, 128, 4, 2>; static constexpr int S = 4, W = 2; };
+
+template <int KIND, int BN>
+static cudaError_t launch_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
+                              int grid, cudaStream_t st) {
+  using P = Pick<KIND, BN>;
+  using C = typename P::C;
+  auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  kern<<<grid, C::THREADS, C::SMEM, st>>>(*tm_w, *tm_b, p);
+  return cudaGetLastError();
+}
+
+template <int KIND, int BN>
+static size_t partials_one(int grid) {
+  using C = typename Pick<KIND, BN>::C;
+  return (size_t)grid * 2 * C::NW * BN * 128 * sizeof(float);
+}
+
+size_t gemm_partials_bytes(int kind, int bn, int grid) {
+  switch (kind * 1000 + bn) {
+    case 1016: return partials_one<1, 16>(grid);
+    case 1032: return partials_one<1, 32>(grid);
+    case 1064: return partials_one<1, 64>(grid);
+    case 1128: return partials_one<1, 128>(grid);
+    case 2016: return partials_one<2, 16>(grid);
+    case 2032: return partials_one<2, 32>(grid);
+    case 2064: return partials_one<2, 64>(grid);
+    case 2128: return partials_one<2, 128>(grid);
+  }
+  return 0;
+}
+
+int gemm_threads(int kind, int bn) {
+  switch (kind * 1000 + bn) {
+    case 1016: return Pick<1, 16>::C::THREADS;
+    case 1032: return Pick<1, 32>::C::THREADS;
+    case 1064: return Pick<1, 64>::C::THREADS;
+    case 1128: return Pick<1, 128>::C::THREADS;
+    case 2016: return Pick<2, 16>::C::THREADS;
+    case 2032: return Pick<2, 32>::C::THREADS;
+    case 2064: return Pick<2, 64>::C::THREADS;
+    case 2128: return Pick<2, 128>::C::THREADS;
+  }
+  return 0;
+}
+
+cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
+                        const GemmParams& p, int grid, cudaStream_t st) {
+  switch (kind * 1000 + bn) {
+    case 1016: return launch_one<1, 16>(tm_w, tm_b, p, grid, st);
+    case 1032: return launch_one<1, 32>(tm_w, tm_b, p, grid, st);
+    case 1064: return launch_one<1, 64>(tm_w, tm_b, p, grid, st);
+    case 1128: return launch_one<1, 128>(tm_w, tm_b, p, grid, st);
+    case 2016: return launch_one<2, 16>(tm_w, tm_b, p, grid, st);
+    case 2032: return launch_one<2, 32>(tm_w, tm_b, p, grid, st);
+    case 2064: return launch_one<2, 64>(tm_w, tm_b, p, grid, st);
+    case 2128: return launch_one<2, 128>(tm_w, tm_b, p, grid, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace moe

@@ -1,0 +1,415 @@
+// Routing, token->expert permutation and weighted combine for the fused FP8
+// DeepSeek-V3 MoE layer.  All kernels here are SIMT and HBM/latency bound;
+// the GEMMs live in gemm_fp8.cu.
+//
+// Reference behaviour followed:
+//   routing   solution/python/kernel.cu:56-200 (CUDA), solution/cuda/moe.cu:178-206
+//             (ATen) and flashinfer trace/templates/moe.py:140-170 (contest definition)
+//   permute   solution/python/kernel.cu:321-351, 503-537, 676-741, 1344-1368, 204-218
+//   combine   solution/python/kernel.cu:809-839 (deterministic finalize)
+#include "kernels.cuh"
+
+namespace moe {
+
+// --------------------------------------------------------------------------
+// Routing + per-CTA histogram of local experts.
+//
+// One warp per token; lane l owns experts 8l..8l+7, so routing group g is
+// lanes 4g..4g+3.  Arithmetic mirrors the reference definition:
+//   s  = 1 / (1 + exp(-x))        exp correctly rounded (evaluated in fp64)
+//   sb = s + bias
+//   group score = sum of the two largest sb in the group; keep the best 4
+//   top-8 of sb inside kept groups
+//   w_k = (s_k / (sum_s + 1e-20)) * routed_scaling_factor
+// The normaliser sum_s adds the selected s values in the order torch's CPU
+// row reduction uses for a [T,256] fp32 tensor (8 lanes of 4 interleaved
+// accumulators, lanes summed last), so weights match the reference's own
+// fp32 arithmetic.  Ties in any top-k go to the lower index.
+// --------------------------------------------------------------------------
+template <bool kFromIds>
+__global__ void __launch_bounds__(kRouteWarps * 32)
+route_hist_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias,
+                  int T, float scaling, int local_offset, int E_l,
+                  int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
+                  int32_t* __restrict__ hist, int* __restrict__ err) {
+  __shared__ int s_hist[kExpertsGlobal];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_hist[e] = 0;
+  __syncthreads();
+
+  const int t_begin = blockIdx.x * kRouteTokensPerCta;
+  const int t_end = min(T, t_begin + kRouteTokensPerCta);
+  for (int t = t_begin + warp; t < t_end; t += kRouteWarps) {
+    int my_id = -1;  // lane k < 8 ends up holding the k-th id (ascending)
+    if constexpr (!kFromIds) {
+      const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExpertsGlobal) + lane * 2;
+      float4 l0 = lp[0], l1 = lp[1];
+      float x[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+      uint4 braw = reinterpret_cast<const uint4*>(bias)[lane];
+      const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&braw);
+      float s[8], sb[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float e = (float)exp(-(double)x[j]);
+        s[j] = __frcp_rn(__fadd_rn(1.0f, e));
+        sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
+      }
+      // ---- group score: sum of the top-2 sb of each 32-expert group
+      float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float v = sb[j];
+        if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+      }
+#pragma unroll
+      for (int off = 1; off <= 2; off <<= 1) {
+        float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+        float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+        float n1, n2;
+        if (m1 >= o1) { n1 = m1; n2 = fmaxf(m2, o1); } else { n1 = o1; n2 = fmaxf(m1, o2); }
+        m1 = n1; m2 = n2;
+      }
+      const float gscore = __fadd_rn(m1, m2);
+      // ---- keep the best 4 groups (ties: lower group)
+      float gs[kGroups];
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
+      unsigned keep = 0;
+#pragma unroll
+      for (int r = 0; r < kTopKGroups; ++r) {
+        int best = -1; float bv = -INFINITY;
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g)
+          if (!((keep >> g) & 1u) && (best < 0 || gs[g] > bv)) { best = g; bv = gs[g]; }
+        keep |= 1u << best;
+      }
+      const bool my_group_kept = (keep >> (lane >> 2)) & 1u;
+      // ---- top-8 experts of sb inside kept groups
+      float cand[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cand[j] = my_group_kept ? sb[j] : -INFINITY;
+      unsigned taken = 0;
+      int sel_e[kTopK];
+      float sel_s[kTopK];
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        int bj = -1; float bv = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) { bj = j; bv = cand[j]; }
+        int be = lane * 8 + bj;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+          float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+          int oe = __shfl_xor_sync(0xffffffffu, be, off);
+          if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+        }
+        float my_s = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) if (be == lane * 8 + j) { taken |= 1u << j; my_s = s[j]; }
+        sel_e[k] = be;
+        sel_s[k] = __shfl_sync(0xffffffffu, my_s, be >> 3);
+      }
+      // ---- sort the 8 picks ascending (all lanes hold the same arrays)
+#pragma unroll
+      for (int a = 1; a < kTopK; ++a)
+#pragma unroll
+        for (int b = a; b > 0; --b)
+          if (sel_e[b] < sel_e[b - 1]) {
+            int te = sel_e[b]; sel_e[b] = sel_e[b - 1]; sel_e[b - 1] = te;
+            float ts = sel_s[b]; sel_s[b] = sel_s[b - 1]; sel_s[b - 1] = ts;
+          }
+      // ---- normaliser in torch's CPU reduction order: lane l (< 8) forms the
+      // vector-lane partial P_l = ((A0+A1)+A2)+A3 with A_q = sum (ascending
+      // expert id) of picks e with e%8 == l and (e/8)%4 == q.
+      float P = 0.f;
+      if (lane < 8) {
+        float A[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k)
+          if ((sel_e[k] & 7) == lane) {
+            int q = (sel_e[k] >> 3) & 3;
+#pragma unroll
+            for (int qq = 0; qq < 4; ++qq) if (qq == q) A[qq] = __fadd_rn(A[qq], sel_s[k]);
+          }
+        P = __fadd_rn(__fadd_rn(__fadd_rn(A[0], A[1]), A[2]), A[3]);
+      }
+      float total = 0.f;
+#pragma unroll
+      for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, P, l));
+      const float denom = __fadd_rn(total, 1e-20f);
+      if (lane < kTopK) {
+        float my_w = 0.f; int my_e = 0;
+#pragma unroll
+        for (int k = 0; k < kTopK; ++k) if (k == lane) { my_e = sel_e[k]; my_w = sel_s[k]; }
+        my_w = __fmul_rn(__fdiv_rn(my_w, denom), scaling);
+        topk_ids[(size_t)t * kTopK + lane] = my_e;
+        topk_w[(size_t)t * kTopK + lane] = my_w;
+        my_id = my_e;
+      }
+    } else {
+      if (lane < kTopK) {
+        my_id = topk_ids[(size_t)t * kTopK + lane];
+        if (my_id < 0 || my_id >= kExpertsGlobal) { raise_error(err, kDevBadExpertId); my_id = -1; }
+      }
+    }
+    if (lane < kTopK && my_id >= 0) {
+      int le = my_id - local_offset;
+      if (le >= 0 && le < E_l) atomicAdd(&s_hist[le], 1);
+    }
+  }
+  __syncthreads();
+  if (hist)
+    for (int e = threadIdx.x; e < E_l; e += blockDim.x)
+      hist[(size_t)blockIdx.x * E_l + e] = s_hist[e];
+}
+
+// --------------------------------------------------------------------------
+// Scan: per-expert row segments, per-(CTA, expert) row bases, GEMM tile
+// lists, and zeroed stream-K counters.  One CTA of 1024 threads.
+// --------------------------------------------------------------------------
+__device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int* total) {
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    int o = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (total) *total = __shfl_sync(0xffffffffu, incl, 31);
+  return incl - v;
+}
+
+// Exclusive scan of n <= 256 values in smem by warp 0 (8 per lane), result in place.
+__device__ void warp0_scan_inplace(int* v, int n, int* total_out) {
+  const int lane = threadIdx.x & 31;
+  int loc[8];
+  int sum = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int idx = lane * 8 + i;
+    loc[i] = idx < n ? v[idx] : 0;
+    sum += loc[i];
+  }
+  int total;
+  int base = warp_exclusive_scan(sum, lane, &total);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    int idx = lane * 8 + i;
+    if (idx < n) v[idx] = base;
+    base += loc[i];
+  }
+  if (lane == 0 && total_out) *total_out = total;
+}
+
+__global__ void __launch_bounds__(1024)
+scan_kernel(int32_t* __restrict__ hist, int NB, int E_l, int32_t* __restrict__ seg_out,
+            int bn1, int bn2, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
+            int32_t* __restrict__ sched, int32_t* __restrict__ counters1, int nt1,
+            int32_t* __restrict__ counters2, int nt2) {
+  __shared__ int s_cnt[kExpertsGlobal];
+  __shared__ int s_seg[kExpertsGlobal + 1];
+  __shared__ int s_t1[kExpertsGlobal];
+  __shared__ int s_t2[kExpertsGlobal];
+  __shared__ int s_tot[3];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int nwarps = blockDim.x >> 5;
+
+  // 1. per-expert totals and per-(block, expert) exclusive bases (in place)
+  for (int e = warp; e < E_l; e += nwarps) {
+    int run = 0;
+    for (int b0 = 0; b0 < NB; b0 += 32) {
+      int b = b0 + lane;
+      int v = b < NB ? hist[(size_t)b * E_l + e] : 0;
+      int tot;
+      int ex = warp_exclusive_scan(v, lane, &tot);
+      if (b < NB) hist[(size_t)b * E_l + e] = run + ex;   // relative to segment start
+      run += tot;
+    }
+    if (lane == 0) s_cnt[e] = run;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    for (int e = lane; e < E_l; e += 32) { s_seg[e] = s_cnt[e]; }
+    __syncwarp();
+    int tot;
+    warp0_scan_inplace(s_seg, E_l, &tot);
+    if (lane == 0) { s_seg[E_l] = tot; s_tot[0] = tot; }
+  } else if (warp == 1) {
+    for (int e = lane; e < E_l; e += 32) s_t1[e] = (s_cnt[e] + bn1 - 1) / bn1;
+    __syncwarp();
+    int tot;
+    warp0_scan_inplace(s_t1, E_l, &tot);
+    if (lane == 0) s_tot[1] = tot;
+  } else if (warp == 2) {
+    for (int e = lane; e < E_l; e += 32) s_t2[e] = (s_cnt[e] + bn2 - 1) / bn2;
+    __syncwarp();
+    int tot;
+    warp0_scan_inplace(s_t2, E_l, &tot);
+    if (lane == 0) s_tot[2] = tot;
+  }
+  __syncthreads();
+  // 2. absolute bases, segment offsets, tile lists
+  for (int i = threadIdx.x; i < NB * E_l; i += blockDim.x) hist[i] += s_seg[i % E_l];
+  for (int e = threadIdx.x; e <= E_l; e += blockDim.x) seg_out[e] = s_seg[e];
+  for (int e = warp; e < E_l; e += nwarps) {
+    const int cnt = s_cnt[e], r0 = s_seg[e];
+    const int n1 = (cnt + bn1 - 1) / bn1, n2 = (cnt + bn2 - 1) / bn2;
+    for (int m = lane; m < n1; m += 32)
+      tiles1[s_t1[e] + m] = make_int4(e, r0 + m * bn1, min(bn1, cnt - m * bn1), 0);
+    for (int m = lane; m < n2; m += 32)
+      tiles2[s_t2[e] + m] = make_int4(e, r0 + m * bn2, min(bn2, cnt - m * bn2), 0);
+  }
+  const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
+  for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
+  for (int i = threadIdx.x; i < units2; i += blockDim.x) counters2[i] = 0;
+  if (threadIdx.x == 0) {
+    sched[0] = s_tot[1];
+    sched[1] = s_tot[2];
+    sched[2] = s_tot[0];
+  }
+}
+
+// --------------------------------------------------------------------------
+// Scatter + gather: rows of local expert e are its tokens in ascending order.
+// Writes inv_row[t,k], row_token[r], the permuted e4m3 rows and their scales.
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+scatter_gather_kernel(const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ bases,
+                      int T, int E_l, int local_offset, int R_cap,
+                      const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
+                      int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
+                      uint8_t* __restrict__ act, float* __restrict__ act_scale) {
+  __shared__ int s_ids[kRouteTokensPerCta * kTopK];
+  __shared__ int s_inv[kRouteTokensPerCta * kTopK];
+  __shared__ int2 s_list[kRouteTokensPerCta * kTopK];
+  __shared__ int s_n;
+  const int t0 = blockIdx.x * kRouteTokensPerCta;
+  const int nt = min(kRouteTokensPerCta, T - t0);
+  if (threadIdx.x == 0) s_n = 0;
+  for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x) {
+    s_ids[i] = topk_ids[(size_t)t0 * kTopK + i] - local_offset;
+    s_inv[i] = -1;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
+    int r = bases[(size_t)blockIdx.x * E_l + e];
+    for (int i = 0; i < nt * kTopK; ++i) {
+      if (s_ids[i] == e) {
+        s_inv[i] = r;
+        int slot = atomicAdd(&s_n, 1);
+        s_list[slot] = make_int2(r, t0 + i / kTopK);
+        ++r;
+      }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x)
+    inv_row[(size_t)t0 * kTopK + i] = s_inv[i];
+  const int n = s_n;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) row_token[s_list[i].x] = s_list[i].y;
+  constexpr int kVec = kHidden / 16;   // 448 uint4 per row
+  for (int i = threadIdx.x; i < n * kVec; i += blockDim.x) {
+    const int2 rt = s_list[i / kVec];
+    const int v = i % kVec;
+    reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden)[v] =
+        __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)rt.y * kHidden) + v);
+  }
+  for (int i = threadIdx.x; i < n * kHiddenBlocks; i += blockDim.x) {
+    const int2 rt = s_list[i / kHiddenBlocks];
+    const int kb = i % kHiddenBlocks;
+    act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Combine: out[t] = sum_k w[t,k] * down[inv[t,k]] over local picks, in
+// ascending expert order, fp32 multiply-then-add (as index_add_ does), then bf16.
+// --------------------------------------------------------------------------
+__global__ void __launch_bounds__(256)
+combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_row,
+               const float* __restrict__ topk_w, int T, __nv_bfloat16* __restrict__ out,
+               float* __restrict__ out_f32) {
+  const int t = blockIdx.x;
+  __shared__ int s_row[kTopK];
+  __shared__ float s_w[kTopK];
+  if (threadIdx.x < kTopK) {
+    s_row[threadIdx.x] = inv_row[(size_t)t * kTopK + threadIdx.x];
+    s_w[threadIdx.x] = topk_w[(size_t)t * kTopK + threadIdx.x];
+  }
+  __syncthreads();
+  for (int v = threadIdx.x; v < kHidden / 4; v += blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int r = s_row[k];
+      if (r < 0) continue;
+      const float w = s_w[k];
+      float4 o = __ldcs(reinterpret_cast<const float4*>(down + (size_t)r * kHidden) + v);
+      acc.x = __fadd_rn(acc.x, __fmul_rn(o.x, w));
+      acc.y = __fadd_rn(acc.y, __fmul_rn(o.y, w));
+      acc.z = __fadd_rn(acc.z, __fmul_rn(o.z, w));
+      acc.w = __fadd_rn(acc.w, __fmul_rn(o.w, w));
+    }
+    if (out_f32) {
+      reinterpret_cast<float4*>(out_f32 + (size_t)t * kHidden)[v] = acc;
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+      uint2 packed;
+      packed.x = *reinterpret_cast<uint32_t*>(&lo);
+      packed.y = *reinterpret_cast<uint32_t*>(&hi);
+      reinterpret_cast<uint2*>(out + (size_t)t * kHidden)[v] = packed;
+    }
+  }
+}
+
+// --------------------------------------------------------------------------
+// Launchers
+// --------------------------------------------------------------------------
+cudaError_t launch_route_hist(bool from_ids, const float* logits, const void* bias, int T,
+                              float scaling, int local_offset, int E_l, int32_t* ids, float* w,
+                              int32_t* hist, int* err, cudaStream_t st) {
+  const int nb = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+  if (nb == 0) return cudaSuccess;
+  if (from_ids)
+    route_hist_kernel<true><<<nb, kRouteWarps * 32, 0, st>>>(
+        logits, static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, ids, w,
+        hist, err);
+  else
+    route_hist_kernel<false><<<nb, kRouteWarps * 32, 0, st>>>(
+        logits, static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, ids, w,
+        hist, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scan(int32_t* hist, int NB, int E_l, int32_t* seg, int bn1, int bn2,
+                        int4* tiles1, int4* tiles2, int32_t* sched, int32_t* counters1, int nt1,
+                        int32_t* counters2, int nt2, cudaStream_t st) {
+  scan_kernel<<<1, 1024, 0, st>>>(hist, NB, E_l, seg, bn1, bn2, tiles1, tiles2, sched, counters1,
+                                  nt1, counters2, nt2);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_scatter_gather(const int32_t* ids, const int32_t* bases, int T, int E_l,
+                                  int local_offset, int R_cap, const void* hidden,
+                                  const float* hs_scale, int32_t* inv_row, int32_t* row_token,
+                                  uint8_t* act, float* act_scale, cudaStream_t st) {
+  const int nb = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+  if (nb == 0) return cudaSuccess;
+  scatter_gather_kernel<<<nb, 256, 0, st>>>(ids, bases, T, E_l, local_offset, R_cap,
+                                            static_cast<const uint8_t*>(hidden), hs_scale,
+                                            inv_row, row_token, act, act_scale);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
+                           void* out, float* out_f32, cudaStream_t st) {
+  if (T == 0) return cudaSuccess;
+  combine_kernel<<<T, 256, 0, st>>>(down, inv_row, w, T, static_cast<__nv_bfloat16*>(out),
+                                    out_f32);
+  return cudaGetLastError();
+}
+
+}  // namespace moe

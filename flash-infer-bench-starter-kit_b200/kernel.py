@@ -1,0 +1,159 @@
+"""Solution entry point: ``kernel(...)`` for
+``moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048``.
+
+Drop-in for the reference's ``solution/python/kernel.py:95-120``: the same 11
+positional arguments, destination-passing style (``output`` is allocated by
+the caller and fully overwritten), work enqueued on the current torch CUDA
+stream with no host synchronisation.  Instead of JIT-compiling a torch
+extension on the first call (``kernel.py:57-92`` of the reference), it calls
+the prebuilt sm_100a library ``libmoe_fp8_ds.so`` through its C ABI.  There
+is no CPU or PyTorch fallback: without the library or a B200 the call raises.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+
+import torch
+
+from . import _lib
+
+H, I, E_GLOBAL, TOP_K = 7168, 2048, 256, 8
+
+_ws_lock = threading.Lock()
+_workspaces: dict[int, torch.Tensor] = {}     # device index -> uint8 workspace (grown on demand)
+
+
+def workspace_bytes(num_tokens: int, num_local_experts: int) -> int:
+    lib = _lib.load()
+    n = ctypes.c_uint64(0)
+    _lib.check(lib.moe_fp8_ds_workspace_size(int(num_tokens), int(num_local_experts), ctypes.byref(n)),
+               "moe_fp8_ds_workspace_size")
+    return int(n.value)
+
+
+def workspace_layout(num_tokens: int, num_local_experts: int) -> _lib.MoeLayout:
+    lib = _lib.load()
+    lay = _lib.MoeLayout()
+    _lib.check(lib.moe_fp8_ds_workspace_layout(int(num_tokens), int(num_local_experts), ctypes.byref(lay)),
+               "moe_fp8_ds_workspace_layout")
+    return lay
+
+
+def get_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The per-device workspace, zero-filled on (re)allocation, at least ``nbytes`` long."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < nbytes:
+            _workspaces.pop(idx, None)
+            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
+            _workspaces[idx] = ws
+        return ws
+
+
+def _check_tensor(name, t, dtype, shape, device):
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if t.dtype != dtype:
+        raise TypeError(f"{name} has dtype {t.dtype}, expected {dtype}")
+    if tuple(t.shape) != tuple(shape):
+        raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _ptr(t):
+    return ctypes.c_void_p(t.data_ptr()) if t is not None else ctypes.c_void_p(0)
+
+
+def build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+               gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+               local_expert_offset, routed_scaling_factor, output, *,
+               topk_ids=None, topk_weights=None, output_f32=None) -> _lib.MoeArgs:
+    """Validate the call's tensors and fill ``struct moe_fp8_ds_args``."""
+    dev = hidden_states.device
+    if dev.type != "cuda":
+        raise ValueError("kernel(...) needs CUDA tensors (no CPU path)")
+    T = hidden_states.shape[0]
+    E_l = gemm1_weights.shape[0]
+    routed = topk_ids is not None
+    if not routed:
+        _check_tensor("routing_logits", routing_logits, torch.float32, (T, E_GLOBAL), dev)
+        _check_tensor("routing_bias", routing_bias, torch.bfloat16, (E_GLOBAL,), dev)
+    else:
+        _check_tensor("topk_ids", topk_ids, torch.int32, (T, TOP_K), dev)
+        _check_tensor("topk_weights", topk_weights, torch.float32, (T, TOP_K), dev)
+    _check_tensor("hidden_states", hidden_states, torch.float8_e4m3fn, (T, H), dev)
+    _check_tensor("hidden_states_scale", hidden_states_scale, torch.float32, (H // 128, T), dev)
+    _check_tensor("gemm1_weights", gemm1_weights, torch.float8_e4m3fn, (E_l, 2 * I, H), dev)
+    _check_tensor("gemm1_weights_scale", gemm1_weights_scale, torch.float32, (E_l, 2 * I // 128, H // 128), dev)
+    _check_tensor("gemm2_weights", gemm2_weights, torch.float8_e4m3fn, (E_l, H, I), dev)
+    _check_tensor("gemm2_weights_scale", gemm2_weights_scale, torch.float32, (E_l, H // 128, I // 128), dev)
+    if output_f32 is not None:
+        _check_tensor("output_f32", output_f32, torch.float32, (T, H), dev)
+    else:
+        _check_tensor("output", output, torch.bfloat16, (T, H), dev)
+    a = _lib.MoeArgs()
+    a.routing_logits = _ptr(routing_logits) if not routed else ctypes.c_void_p(0)
+    a.routing_bias = _ptr(routing_bias) if not routed else ctypes.c_void_p(0)
+    a.hidden_states = _ptr(hidden_states)
+    a.hidden_states_scale = _ptr(hidden_states_scale)
+    a.gemm1_weights = _ptr(gemm1_weights)
+    a.gemm1_weights_scale = _ptr(gemm1_weights_scale)
+    a.gemm2_weights = _ptr(gemm2_weights)
+    a.gemm2_weights_scale = _ptr(gemm2_weights_scale)
+    a.output = _ptr(output) if output_f32 is None else ctypes.c_void_p(0)
+    a.num_tokens = int(T)
+    a.num_local_experts = int(E_l)
+    a.local_expert_offset = int(local_expert_offset)
+    a.routed_scaling_factor = float(routed_scaling_factor)
+    a.topk_ids = _ptr(topk_ids)
+    a.topk_weights = _ptr(topk_weights)
+    a.output_f32 = _ptr(output_f32)
+    return a
+
+
+def run_with_workspace(args: _lib.MoeArgs, ws: torch.Tensor, stream: int | None = None,
+                       routed: bool = False) -> None:
+    lib = _lib.load()
+    if stream is None:
+        stream = torch.cuda.current_stream().cuda_stream
+    fn = lib.moe_fp8_ds_run_routed if routed else lib.moe_fp8_ds_run
+    _lib.check(fn(ctypes.byref(args), ctypes.c_void_p(ws.data_ptr()), ctypes.c_uint64(ws.numel()),
+                  ctypes.c_void_p(stream)), fn.__name__)
+
+
+def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+           gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+           local_expert_offset, routed_scaling_factor, output):
+    """Fused FP8 block-scale MoE forward with DeepSeek-V3 routing (DPS: writes ``output``)."""
+    args = build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                      local_expert_offset, routed_scaling_factor, output)
+    with torch.cuda.device(hidden_states.device):
+        ws = get_workspace(hidden_states.device,
+                           workspace_bytes(args.num_tokens, args.num_local_experts))
+        run_with_workspace(args, ws)
+
+
+def read_device_error(device: torch.device | None = None) -> int:
+    """Synchronise the current stream and return (and clear) the device error code of the
+    workspace used on ``device``; 0 means no device-side error since the last read."""
+    lib = _lib.load()
+    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    ws = _workspaces.get(idx)
+    if ws is None:
+        return 0
+    code = ctypes.c_int32(0)
+    with torch.cuda.device(idx):
+        st = lib.moe_fp8_ds_read_device_error(ctypes.c_void_p(ws.data_ptr()),
+                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
+                                              ctypes.byref(code))
+    if st not in (_lib.MOE_OK, _lib.MOE_ERR_DEVICE_TIMEOUT, _lib.MOE_ERR_DEVICE_FAULT):
+        _lib.check(st, "moe_fp8_ds_read_device_error")
+    return int(code.value)
