@@ -107,7 +107,8 @@ class ClockSampler:
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4)
+                          if len(r) > 5 + i and r[5 + i].strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
                 "reasons": reasons, "samples": len(rows)}
 
@@ -160,9 +161,9 @@ def stage_times(L, fn, steps, flush):
     per = {s: [] for s in STAGES}
     for _ in range(steps):
         evs = [torch.cuda.Event(enable_timing=True) for _ in range(7)]
-        arr = (ctypes.c_void_p * 7)(*[ctypes.c_void_p(e.cuda_event) for e in evs])
         for e in evs:          # materialise the events on this device
             e.record()
+        arr = (ctypes.c_void_p * 7)(*[ctypes.c_void_p(e.cuda_event) for e in evs])
         flush.fill_(3)
         torch.cuda.synchronize()
         L.check(lib.moe_fp8_ds_set_stage_events(arr, 7), "set_stage_events")
@@ -284,7 +285,7 @@ def main():
     L = sys.modules["fib_b200._lib"]
     hbm_peak, peak_kind = measured_peaks()
 
-    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep else []
+    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep not in ("", "none") else []
     T_max = max([T] + sweep_T)
     # Each rank holds the 32 experts of one expert-parallel slot (offset 32*rank).
     offset = (E_l * rank) % 256
@@ -304,9 +305,8 @@ def main():
     if world > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        ts = time_steps(fn, a.steps, a.warmup, flush)
-    clocks = clk.summary()
+    clk = ClockSampler(local_rank).__enter__()
+    ts = time_steps(fn, a.steps, a.warmup, flush)
     ms = sum(ts) / len(ts)
     if world > 1:
         t = torch.tensor([ms], device=dev)
@@ -328,6 +328,10 @@ def main():
                       "active_experts": na, "assignments": Rs, "hbm_gbs": bb / (mss * 1e-3) / 1e9,
                       "hbm_frac": bb / (mss * 1e-3) / 1e9 / hbm_peak,
                       "fp8_tflops": Rs * FLOPS_PER_ASSIGNMENT / (mss * 1e-3) / 1e12})
+
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
+    clocks["window"] = "headline + sweep timed regions"
 
     cpu = None
     if rank == 0 and not a.no_cpu_baseline:

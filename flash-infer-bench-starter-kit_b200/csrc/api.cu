@@ -73,7 +73,7 @@ int pick_bn(int T, int E_l) {
 struct Plan {
   moe_fp8_ds_layout pub;
   int T, E_l, NB, R_cap, bn1, bn2, grid, max_mt1, max_mt2;
-  uint64_t hist, tiles1, tiles2, sched, counters1, counters2, partials1, partials2;
+  uint64_t tiles1, tiles2, sched, counters1, counters2, partials1, partials2;
 };
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
@@ -82,7 +82,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   memset(P, 0, sizeof(*P));
   P->T = T;
   P->E_l = E_l;
-  P->NB = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+  P->NB = (T + kPermBlock - 1) / kPermBlock;
   P->R_cap = T * (E_l < kTopK ? E_l : kTopK);
   P->bn1 = g_bn_override[0] ? g_bn_override[0] : pick_bn(T, E_l);
   P->bn2 = g_bn_override[1] ? g_bn_override[1] : pick_bn(T, E_l);
@@ -100,7 +100,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.topk_ids = take((uint64_t)T * kTopK * 4);
   P->pub.topk_weights = take((uint64_t)T * kTopK * 4);
   P->pub.inv_row = take((uint64_t)T * kTopK * 4);
-  P->hist = take((uint64_t)P->NB * E_l * 4);
+  P->pub.block_masks = take((uint64_t)P->NB * E_l * 4);
+  P->pub.block_bases = take((uint64_t)P->NB * E_l * 4);
   P->pub.seg_offsets = take((uint64_t)(E_l + 1) * 4);
   P->tiles1 = take((uint64_t)P->max_mt1 * 16);
   P->tiles2 = take((uint64_t)P->max_mt2 * 16);
@@ -108,8 +109,6 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->pub.row_token = take(R * 4);
-  P->pub.act = take(R * kHidden);
-  P->pub.act_scale = take(R * kHiddenBlocks * 4);
   P->pub.inter = take(2 * R * kInter);
   P->pub.inter_scale = take(R * kInterBlocks * 4);
   P->pub.down = take(R * kHidden * 4);
@@ -172,7 +171,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   int32_t* ids = routed ? const_cast<int32_t*>(a->topk_ids) : reinterpret_cast<int32_t*>(at(P.pub.topk_ids));
   float* wts = routed ? const_cast<float*>(a->topk_weights) : reinterpret_cast<float*>(at(P.pub.topk_weights));
   int32_t* inv = reinterpret_cast<int32_t*>(at(P.pub.inv_row));
-  int32_t* hist = reinterpret_cast<int32_t*>(at(P.hist));
+  uint32_t* masks = reinterpret_cast<uint32_t*>(at(P.pub.block_masks));
+  int32_t* bases = reinterpret_cast<int32_t*>(at(P.pub.block_bases));
   int32_t* seg = reinterpret_cast<int32_t*>(at(P.pub.seg_offsets));
   int4* tiles1 = reinterpret_cast<int4*>(at(P.tiles1));
   int4* tiles2 = reinterpret_cast<int4*>(at(P.tiles2));
@@ -180,8 +180,6 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   int32_t* cnt1 = reinterpret_cast<int32_t*>(at(P.counters1));
   int32_t* cnt2 = reinterpret_cast<int32_t*>(at(P.counters2));
   int32_t* row_token = reinterpret_cast<int32_t*>(at(P.pub.row_token));
-  uint8_t* act = at(P.pub.act);
-  float* act_scale = reinterpret_cast<float*>(at(P.pub.act_scale));
   uint8_t* inter = at(P.pub.inter);
   float* inter_scale = reinterpret_cast<float*>(at(P.pub.inter_scale));
   float* down = reinterpret_cast<float*>(at(P.pub.down));
@@ -189,27 +187,27 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
 
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
   if (!encode_2d(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128) ||
-      !encode_2d(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
+      !encode_2d(&tm_b1, a->hidden_states, kHidden, (uint64_t)T, 1) ||
       !encode_2d(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128) ||
       !encode_2d(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2)))
     return MOE_ERR_INVALID_ARGUMENT;
 
   cudaError_t ce;
   mark_stage(0, s);
-  ce = launch_route_hist(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
-                         a->local_expert_offset, E_l, ids, wts, hist, err, s);
+  ce = launch_route(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
+                    a->local_expert_offset, E_l, ids, wts, masks, err, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
   mark_stage(1, s);
-  ce = launch_scan(hist, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1, kInter / 128,
-                   cnt2, kHidden / 128, s);
+  ce = launch_scan(masks, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
+                   kInter / 128, cnt2, kHidden / 128, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
   mark_stage(2, s);
-  ce = launch_scatter_gather(ids, hist, T, E_l, a->local_expert_offset, P.R_cap, a->hidden_states,
-                             a->hidden_states_scale, inv, row_token, act, act_scale, s);
+  ce = launch_scatter(ids, masks, bases, T, E_l, a->local_expert_offset, inv, row_token, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   GemmParams g1{};
-  g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale; g1.b_scale = act_scale;
+  g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
+  g1.b_scale = a->hidden_states_scale; g1.b_scale_stride = T; g1.row_token = row_token;
   g1.counters = cnt1; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
@@ -217,7 +215,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   GemmParams g2{};
-  g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale; g2.b_scale = inter_scale;
+  g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale;
+  g2.b_scale = inter_scale; g2.b_scale_stride = P.R_cap; g2.row_token = nullptr;
   g2.counters = cnt2; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
@@ -281,9 +280,9 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int3
   int st = device_info(&dev);
   if (st != MOE_OK) return st;
   // No local experts (E_l = 0, no histogram): routing only.
-  cudaError_t ce = launch_route_hist(false, routing_logits, routing_bias, num_tokens,
-                                     routed_scaling_factor, 0, 0, topk_ids, topk_weights,
-                                     nullptr, nullptr, static_cast<cudaStream_t>(stream));
+  cudaError_t ce = launch_route(false, routing_logits, routing_bias, num_tokens,
+                                routed_scaling_factor, 0, 0, topk_ids, topk_weights, nullptr,
+                                nullptr, static_cast<cudaStream_t>(stream));
   return ce == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 

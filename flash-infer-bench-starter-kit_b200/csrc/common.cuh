@@ -27,9 +27,9 @@ constexpr int kTopKGroups = 4;
 constexpr int kGroupSize = kExpertsGlobal / kGroups;   // 32
 constexpr float kFp8Max = 448.0f;
 
-// Routing kernel: tokens per CTA (one warp per token, kRouteWarps warps, loop).
-constexpr int kRouteTokensPerCta = 64;
-constexpr int kRouteWarps = 8;
+// Permutation block: tokens per routing CTA (one warp per token); the
+// per-block expert masks are 32-bit.
+constexpr int kPermBlock = 32;
 
 // A bounded wait gives up after this many nanoseconds and raises the
 // device error word; every kernel here finishes in well under a second.
@@ -60,6 +60,17 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 
 __device__ __forceinline__ void raise_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
+}
+
+// ---- programmatic dependent launch --------------------------------------
+// Wait until the preceding kernel in the stream has completed and its writes
+// are visible (no-op when launched without the PDL attribute).
+__device__ __forceinline__ void griddep_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Allow the next kernel in the stream to begin launching its CTAs.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
 // ---- mbarrier -------------------------------------------------------------
@@ -139,6 +150,20 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// 2D gather of four rows (tile::gather4): x = first column, rows r0..r3;
+// the tensor map's box is 128 columns x 1 row and the four rows land as
+// consecutive 128-byte rows at smem_dst.
+__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
+                                            int32_t x, int32_t r0, int32_t r1, int32_t r2, int32_t r3,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1), "r"(r2),
+      "r"(r3), "l"(policy)
+      : "memory");
 }
 
 // ---- tcgen05 / TMEM -------------------------------------------------------
@@ -242,6 +267,23 @@ __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
 __device__ __forceinline__ float e4m3_to_f32(uint8_t b) {
   __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(b), __NV_E4M3);
   return __half2float(__half(hr));
+}
+
+// Launch with the programmatic-stream-serialization attribute (PDL).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
 }  // namespace moe

@@ -49,13 +49,16 @@ struct GemmCfg {
   static constexpr int W_TILE = 128 * 128;
   static constexpr int B_TILE = MMA_N * 128;
   static constexpr int STAGE = NW * W_TILE + B_TILE;
-  static constexpr int TMEM_USED = 2 * NW * MMA_N;
+  static constexpr int NBUF = 4 * NW * MMA_N <= 512 ? 4 : 2;   // TMEM partial buffers
+  static constexpr int TMEM_USED = NBUF * NW * MMA_N;
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64
                                  : TMEM_USED <= 128 ? 128 : TMEM_USED <= 256 ? 256 : 512;
   static constexpr int NEPI = 128 * NWG;
   static constexpr int THREADS = 64 + NEPI;
   static constexpr int CPW = BN / NWG;                      // token columns per warpgroup
-  static constexpr int AUX = 2048 + 2 * BN * 4 + NWG * 4 * CPW * 4;
+  static constexpr int SLOT = BN + NW;                      // per-iteration scales: tokens + weight
+  static constexpr int RING = 3;                            // scale slots (prefetch distance 2)
+  static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4 + BN * 4;
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
   static_assert(TMEM_USED <= 512, "TMEM budget");
   static_assert(CPW % 16 == 0 || (KIND == 2 && CPW % 8 == 0), "column chunking");
@@ -90,24 +93,27 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint64_t* full = reinterpret_cast<uint64_t*>(aux);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* drain = tempty + 2;
+  uint64_t* tempty = tfull + C::NBUF;
+  uint64_t* drain = tempty + C::NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = const_cast<int*>(abort_flag) + 1;     // [NWG]
-  float* sbuf = reinterpret_cast<float*>(aux + 2048);      // [2][BN] token-column scales
-  float* samax = sbuf + 2 * BN;                            // [NWG][4][CPW]
+  float* sring = reinterpret_cast<float*>(aux + 2048);     // [RING][SLOT] scales per iteration
+  float* samax = sring + C::RING * C::SLOT;                // [NWG][4][CPW]
+  int* s_tok = reinterpret_cast<int*>(samax + NWG * 4 * C::CPW);   // [BN] GEMM1 token rows
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  griddep_wait();                   // routing/permutation (or GEMM1) results are visible
+  griddep_launch_dependents();
   const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KB);
   if (sch.it0 >= sch.it1) return;   // uniform: this CTA has no work
   const int n_iter = sch.it1 - sch.it0;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-    for (int b = 0; b < 2; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NWG * 4); }
+    for (int b = 0; b < C::NBUF; ++b) { mbar_init(&tfull[b], 1); mbar_init(&tempty[b], NWG * 4); }
     mbar_init(drain, 1);
     *const_cast<int*>(abort_flag) = 0;
     fence_mbar_init();
@@ -121,36 +127,54 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    if (elect_one_lane()) {
-      const uint64_t pol_w = l2_policy_evict_first();
-      const uint64_t pol_b = l2_policy_evict_last();
-      int issued = 0;
-      bool ok = true;
-      for (int i = 0; i < n_iter && ok; ++i) {
-        const int it = sch.it0 + i;
-        const int u = it / C::KB, kb = it % C::KB;
-        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
-        const int4 tile = p.tiles[mt];
-        const int s = i % STAGES;
-        if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], C::STAGE);
-        uint8_t* st = smem + s * C::STAGE;
-        const int x = kb * 128;
-        const int wrow = tile.x * C::W_ROWS + nt * 128;
-        tma_load_2d(&tm_w, &full[s], st, x, wrow, pol_w);
-        if (KIND == 1) tma_load_2d(&tm_w, &full[s], st + C::W_TILE, x, wrow + kInter, pol_w);
-        tma_load_2d(&tm_b, &full[s], st + C::NW * C::W_TILE, x,
-                    KIND == 1 ? tile.y : 2 * tile.y, pol_b);
-        ++issued;
+    // Lane 0 issues the TMA copies; for GEMM1 the whole warp first stages the
+    // tile's source-token ids, which the row gathers (tile::gather4) read.
+    const uint64_t pol_w = l2_policy_evict_first();
+    const uint64_t pol_b = l2_policy_evict_last();
+    int issued = 0;
+    bool ok = true;
+    for (int i = 0; i < n_iter; ++i) {
+      const int it = sch.it0 + i;
+      const int u = it / C::KB, kb = it % C::KB;
+      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      const int4 tile = p.tiles[mt];
+      if (KIND == 1 && (i == 0 || kb == 0)) {
+        for (int j = lane; j < BN; j += 32)
+          s_tok[j] = __ldg(p.row_token + tile.y + (j < tile.z ? j : 0));
+        __syncwarp();
       }
-      if (!ok) {
-        raise_error(p.err, kDevTimeoutProducer);
-        // Let copies already in flight land before the CTA exits.
-        for (int i = max(0, issued - STAGES); i < issued; ++i) {
-          const unsigned long long t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
-                 globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
+      const int s = i % STAGES;
+      if (lane == 0) {
+        ok = mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag);
+        if (ok) {
+          mbar_arrive_expect_tx(&full[s], C::STAGE);
+          uint8_t* st = smem + s * C::STAGE;
+          const int x = kb * 128;
+          const int wrow = tile.x * C::W_ROWS + nt * 128;
+          tma_load_2d(&tm_w, &full[s], st, x, wrow, pol_w);
+          if (KIND == 1) {
+            tma_load_2d(&tm_w, &full[s], st + C::W_TILE, x, wrow + kInter, pol_w);
+            uint8_t* dst = st + C::NW * C::W_TILE;
+#pragma unroll
+            for (int g = 0; g < BN / 4; ++g)
+              tma_gather4(&tm_b, &full[s], dst + g * 512, x, s_tok[4 * g], s_tok[4 * g + 1],
+                          s_tok[4 * g + 2], s_tok[4 * g + 3], pol_b);
+          } else {
+            tma_load_2d(&tm_b, &full[s], st + C::NW * C::W_TILE, x, 2 * tile.y, pol_b);
+          }
+          ++issued;
         }
+      }
+      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      if (!ok) break;
+    }
+    if (!ok && lane == 0) {
+      raise_error(p.err, kDevTimeoutProducer);
+      // Let copies already in flight land before the CTA exits.
+      for (int i = max(0, issued - STAGES); i < issued; ++i) {
+        const unsigned long long t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+               globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
       }
     }
   } else if (warp == 1) {
@@ -160,9 +184,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint32_t smem_base = smem_u32(smem);
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
-        const int s = i % STAGES, b = i & 1;
+        const int s = i % STAGES, b = i % C::NBUF;
         if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
-        if (!mbar_wait_bounded(&tempty[b], ((i >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        if (!mbar_wait_bounded(&tempty[b], ((i / C::NBUF) & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = smem_base + s * C::STAGE;
         const uint64_t bdesc = make_sdesc_sw128(st + C::NW * C::W_TILE);
@@ -196,19 +220,36 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     int seg_kb0 = 0;
     int4 tile = make_int4(0, 0, 0, 0);
 
-    auto scale_for = [&](int it, int j) -> float {
-      const int u = it / C::KB, kb = it % C::KB;
-      const int4 tl = p.tiles[u % sch.n_mt];
-      return j < tl.z ? __ldg(p.b_scale + (size_t)kb * p.R_cap + tl.y + j) : 0.f;
+    // Scales of iteration i live in ring slot i % RING: [0, BN) token-column
+    // scales, [BN, BN+NW) weight-block scales.  Thread et < BN+NW loads its
+    // entry two iterations ahead, so the loads never sit on the critical path.
+    int pf_unit = -1, pf_col = -1, pf_e = 0, pf_nt = 0;
+    auto fetch = [&](int i_t) -> float {
+      const int it_t = sch.it0 + i_t;
+      const int u_t = it_t / C::KB, kb_t = it_t % C::KB;
+      if (u_t != pf_unit) {
+        pf_unit = u_t;
+        const int4 tl = p.tiles[u_t % sch.n_mt];
+        pf_e = tl.x;
+        pf_nt = u_t / sch.n_mt;
+        pf_col = -1;
+        if (et < BN && et < tl.z) pf_col = KIND == 1 ? __ldg(p.row_token + tl.y + et) : tl.y + et;
+      }
+      if (et < BN) return pf_col >= 0 ? __ldg(p.b_scale + (size_t)kb_t * p.b_scale_stride + pf_col) : 0.f;
+      const int w = et - BN;
+      const int nb = KIND == 1 ? pf_nt + w * (kInter / 128) : pf_nt;
+      return __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
     };
-    if (et < BN) sbuf[et] = scale_for(sch.it0, et);
+    const bool loader = et < C::SLOT;
+    for (int i_t = 0; i_t < 2 && i_t < n_iter; ++i_t)
+      if (loader) sring[i_t * C::SLOT + et] = fetch(i_t);
     named_bar_sync(1, C::NEPI);
 
     for (int i = 0; i < n_iter; ++i) {
       const int it = sch.it0 + i;
       const int u = it / C::KB, kb = it % C::KB;
       const int nt = u / sch.n_mt, mt = u % sch.n_mt;
-      const int b = i & 1;
+      const int b = i % C::NBUF;
       if (i == 0 || kb == 0) {
         tile = p.tiles[mt];
         seg_kb0 = kb;
@@ -217,17 +258,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
           for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
       }
-      const float pre = (i + 1 < n_iter && et < BN) ? scale_for(it + 1, et) : 0.f;
+      const float pre = (loader && i + 2 < n_iter) ? fetch(i + 2) : 0.f;
+      const float* sb = sring + (i % C::RING) * C::SLOT;
       float wsc[C::NW];
 #pragma unroll
-      for (int w = 0; w < C::NW; ++w) {
-        const int nb = KIND == 1 ? nt + w * (kInter / 128) : nt;
-        wsc[w] = __ldg(p.w_scale + ((size_t)tile.x * (C::W_ROWS / 128) + nb) * C::KB + kb);
-      }
-      const bool got = mbar_wait_bounded(&tfull[b], (i >> 1) & 1, abort_flag);
+      for (int w = 0; w < C::NW; ++w) wsc[w] = sb[BN + w];
+      const bool got = mbar_wait_bounded(&tfull[b], (i / C::NBUF) & 1, abort_flag);
       if (got) {
         tc_fence_after();
-        const float* sb = sbuf + b * BN;   // buffer index = i & 1
 #pragma unroll
         for (int w = 0; w < C::NW; ++w) {
           const uint32_t col0 = (uint32_t)(b * C::NW * C::MMA_N + w * C::MMA_N);
@@ -262,7 +300,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
-      if (et < BN) sbuf[((i + 1) & 1) * BN + et] = pre;
+      if (loader && i + 2 < n_iter) sring[((i + 2) % C::RING) * C::SLOT + et] = pre;
       named_bar_sync(1, C::NEPI);
       if (*abort_flag) break;
 
@@ -381,8 +419,7 @@ static cudaError_t launch_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, 
   auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  kern<<<grid, C::THREADS, C::SMEM, st>>>(*tm_w, *tm_b, p);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
 }
 
 template <int KIND, int BN>

@@ -12,10 +12,11 @@
 namespace moe {
 
 // --------------------------------------------------------------------------
-// Routing + per-CTA histogram of local experts.
+// Routing + per-block token masks of local experts.
 //
-// One warp per token; lane l owns experts 8l..8l+7, so routing group g is
-// lanes 4g..4g+3.  Arithmetic mirrors the reference definition:
+// One warp per token, 32 tokens per CTA ("permutation block"); lane l owns
+// experts 8l..8l+7, so routing group g is lanes 4g..4g+3.  Arithmetic mirrors
+// the reference definition:
 //   s  = 1 / (1 + exp(-x))        exp correctly rounded (evaluated in fp64)
 //   sb = s + bias
 //   group score = sum of the two largest sb in the group; keep the best 4
@@ -25,22 +26,27 @@ namespace moe {
 // row reduction uses for a [T,256] fp32 tensor (8 lanes of 4 interleaved
 // accumulators, lanes summed last), so weights match the reference's own
 // fp32 arithmetic.  Ties in any top-k go to the lower index.
+//
+// masks[b][e] has bit w set when token 32b+w picked local expert e; the
+// scan turns popcounts into row offsets, the scatter turns masked
+// popcounts into each token's rank inside its expert (ascending tokens).
 // --------------------------------------------------------------------------
 template <bool kFromIds>
-__global__ void __launch_bounds__(kRouteWarps * 32)
-route_hist_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias,
-                  int T, float scaling, int local_offset, int E_l,
-                  int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
-                  int32_t* __restrict__ hist, int* __restrict__ err) {
-  __shared__ int s_hist[kExpertsGlobal];
+__global__ void __launch_bounds__(kPermBlock * 32)
+route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias,
+             int T, float scaling, int local_offset, int E_l,
+             int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
+             uint32_t* __restrict__ masks, int* __restrict__ err) {
+  __shared__ uint32_t s_mask[kExpertsGlobal];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_hist[e] = 0;
+  griddep_wait();
+  griddep_launch_dependents();
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
   __syncthreads();
 
-  const int t_begin = blockIdx.x * kRouteTokensPerCta;
-  const int t_end = min(T, t_begin + kRouteTokensPerCta);
-  for (int t = t_begin + warp; t < t_end; t += kRouteWarps) {
+  const int t = blockIdx.x * kPermBlock + warp;
+  if (t < T) {
     int my_id = -1;  // lane k < 8 ends up holding the k-th id (ascending)
     if constexpr (!kFromIds) {
       const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExpertsGlobal) + lane * 2;
@@ -156,13 +162,13 @@ route_hist_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restr
     }
     if (lane < kTopK && my_id >= 0) {
       int le = my_id - local_offset;
-      if (le >= 0 && le < E_l) atomicAdd(&s_hist[le], 1);
+      if (le >= 0 && le < E_l) atomicOr(&s_mask[le], 1u << warp);
     }
   }
   __syncthreads();
-  if (hist)
+  if (masks)
     for (int e = threadIdx.x; e < E_l; e += blockDim.x)
-      hist[(size_t)blockIdx.x * E_l + e] = s_hist[e];
+      masks[(size_t)blockIdx.x * E_l + e] = s_mask[e];
 }
 
 // --------------------------------------------------------------------------
@@ -203,7 +209,8 @@ __device__ void warp0_scan_inplace(int* v, int n, int* total_out) {
 }
 
 __global__ void __launch_bounds__(1024)
-scan_kernel(int32_t* __restrict__ hist, int NB, int E_l, int32_t* __restrict__ seg_out,
+scan_kernel(const uint32_t* __restrict__ masks, int32_t* __restrict__ bases, int NB, int E_l,
+            int32_t* __restrict__ seg_out,
             int bn1, int bn2, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
             int32_t* __restrict__ sched, int32_t* __restrict__ counters1, int nt1,
             int32_t* __restrict__ counters2, int nt2) {
@@ -216,15 +223,17 @@ scan_kernel(int32_t* __restrict__ hist, int NB, int E_l, int32_t* __restrict__ s
   const int warp = threadIdx.x >> 5;
   const int nwarps = blockDim.x >> 5;
 
-  // 1. per-expert totals and per-(block, expert) exclusive bases (in place)
+  griddep_wait();
+  griddep_launch_dependents();
+  // 1. per-expert totals and per-(block, expert) exclusive bases
   for (int e = warp; e < E_l; e += nwarps) {
     int run = 0;
     for (int b0 = 0; b0 < NB; b0 += 32) {
       int b = b0 + lane;
-      int v = b < NB ? hist[(size_t)b * E_l + e] : 0;
+      int v = b < NB ? __popc(masks[(size_t)b * E_l + e]) : 0;
       int tot;
       int ex = warp_exclusive_scan(v, lane, &tot);
-      if (b < NB) hist[(size_t)b * E_l + e] = run + ex;   // relative to segment start
+      if (b < NB) bases[(size_t)b * E_l + e] = run + ex;   // relative to segment start
       run += tot;
     }
     if (lane == 0) s_cnt[e] = run;
@@ -251,7 +260,7 @@ scan_kernel(int32_t* __restrict__ hist, int NB, int E_l, int32_t* __restrict__ s
   }
   __syncthreads();
   // 2. absolute bases, segment offsets, tile lists
-  for (int i = threadIdx.x; i < NB * E_l; i += blockDim.x) hist[i] += s_seg[i % E_l];
+  for (int i = threadIdx.x; i < NB * E_l; i += blockDim.x) bases[i] += s_seg[i % E_l];
   for (int e = threadIdx.x; e <= E_l; e += blockDim.x) seg_out[e] = s_seg[e];
   for (int e = warp; e < E_l; e += nwarps) {
     const int cnt = s_cnt[e], r0 = s_seg[e];
@@ -272,55 +281,28 @@ scan_kernel(int32_t* __restrict__ hist, int NB, int E_l, int32_t* __restrict__ s
 }
 
 // --------------------------------------------------------------------------
-// Scatter + gather: rows of local expert e are its tokens in ascending order.
-// Writes inv_row[t,k], row_token[r], the permuted e4m3 rows and their scales.
+// Scatter: rows of local expert e are its tokens in ascending order; the rank
+// of token 32b+w inside expert e is popc(masks[b][e] & ((1<<w)-1)).
+// Writes inv_row[t,k] (row or -1) and row_token[row].
 // --------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-scatter_gather_kernel(const int32_t* __restrict__ topk_ids, const int32_t* __restrict__ bases,
-                      int T, int E_l, int local_offset, int R_cap,
-                      const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
-                      int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
-                      uint8_t* __restrict__ act, float* __restrict__ act_scale) {
-  __shared__ int s_ids[kRouteTokensPerCta * kTopK];
-  __shared__ int s_inv[kRouteTokensPerCta * kTopK];
-  __shared__ int2 s_list[kRouteTokensPerCta * kTopK];
-  __shared__ int s_n;
-  const int t0 = blockIdx.x * kRouteTokensPerCta;
-  const int nt = min(kRouteTokensPerCta, T - t0);
-  if (threadIdx.x == 0) s_n = 0;
-  for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x) {
-    s_ids[i] = topk_ids[(size_t)t0 * kTopK + i] - local_offset;
-    s_inv[i] = -1;
+__global__ void __launch_bounds__(kPermBlock * kTopK)
+scatter_kernel(const int32_t* __restrict__ topk_ids, const uint32_t* __restrict__ masks,
+               const int32_t* __restrict__ bases, int T, int E_l, int local_offset,
+               int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int i = blockIdx.x * kPermBlock * kTopK + threadIdx.x;   // (t, k) pair
+  const int t = i / kTopK;
+  if (t >= T) return;
+  const int le = topk_ids[i] - local_offset;
+  int row = -1;
+  if (le >= 0 && le < E_l) {
+    const int w = t - blockIdx.x * kPermBlock;
+    const size_t be = (size_t)blockIdx.x * E_l + le;
+    row = bases[be] + __popc(masks[be] & ((1u << w) - 1u));
+    row_token[row] = t;
   }
-  __syncthreads();
-  for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
-    int r = bases[(size_t)blockIdx.x * E_l + e];
-    for (int i = 0; i < nt * kTopK; ++i) {
-      if (s_ids[i] == e) {
-        s_inv[i] = r;
-        int slot = atomicAdd(&s_n, 1);
-        s_list[slot] = make_int2(r, t0 + i / kTopK);
-        ++r;
-      }
-    }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < nt * kTopK; i += blockDim.x)
-    inv_row[(size_t)t0 * kTopK + i] = s_inv[i];
-  const int n = s_n;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) row_token[s_list[i].x] = s_list[i].y;
-  constexpr int kVec = kHidden / 16;   // 448 uint4 per row
-  for (int i = threadIdx.x; i < n * kVec; i += blockDim.x) {
-    const int2 rt = s_list[i / kVec];
-    const int v = i % kVec;
-    reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden)[v] =
-        __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)rt.y * kHidden) + v);
-  }
-  for (int i = threadIdx.x; i < n * kHiddenBlocks; i += blockDim.x) {
-    const int2 rt = s_list[i / kHiddenBlocks];
-    const int kb = i % kHiddenBlocks;
-    act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
-  }
+  inv_row[i] = row;
 }
 
 // --------------------------------------------------------------------------
@@ -331,6 +313,8 @@ __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_row,
                const float* __restrict__ topk_w, int T, __nv_bfloat16* __restrict__ out,
                float* __restrict__ out_f32) {
+  griddep_wait();
+  griddep_launch_dependents();
   const int t = blockIdx.x;
   __shared__ int s_row[kTopK];
   __shared__ float s_w[kTopK];
@@ -366,50 +350,43 @@ combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_r
 }
 
 // --------------------------------------------------------------------------
-// Launchers
+// Launchers (programmatic dependent launch: each kernel may start while the
+// previous one drains; griddepcontrol.wait orders its reads)
 // --------------------------------------------------------------------------
-cudaError_t launch_route_hist(bool from_ids, const float* logits, const void* bias, int T,
-                              float scaling, int local_offset, int E_l, int32_t* ids, float* w,
-                              int32_t* hist, int* err, cudaStream_t st) {
-  const int nb = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
+                         float scaling, int local_offset, int E_l, int32_t* ids, float* w,
+                         uint32_t* masks, int* err, cudaStream_t st) {
+  const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
+  const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(bias);
   if (from_ids)
-    route_hist_kernel<true><<<nb, kRouteWarps * 32, 0, st>>>(
-        logits, static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, ids, w,
-        hist, err);
-  else
-    route_hist_kernel<false><<<nb, kRouteWarps * 32, 0, st>>>(
-        logits, static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, ids, w,
-        hist, err);
-  return cudaGetLastError();
+    return launch_pdl(route_kernel<true>, dim3(nb), dim3(kPermBlock * 32), 0, st, logits, b, T,
+                      scaling, local_offset, E_l, ids, w, masks, err);
+  return launch_pdl(route_kernel<false>, dim3(nb), dim3(kPermBlock * 32), 0, st, logits, b, T,
+                    scaling, local_offset, E_l, ids, w, masks, err);
 }
 
-cudaError_t launch_scan(int32_t* hist, int NB, int E_l, int32_t* seg, int bn1, int bn2,
-                        int4* tiles1, int4* tiles2, int32_t* sched, int32_t* counters1, int nt1,
-                        int32_t* counters2, int nt2, cudaStream_t st) {
-  scan_kernel<<<1, 1024, 0, st>>>(hist, NB, E_l, seg, bn1, bn2, tiles1, tiles2, sched, counters1,
-                                  nt1, counters2, nt2);
-  return cudaGetLastError();
+cudaError_t launch_scan(const uint32_t* masks, int32_t* bases, int NB, int E_l, int32_t* seg,
+                        int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
+                        int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st) {
+  return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks, bases, NB, E_l, seg, bn1, bn2,
+                    tiles1, tiles2, sched, counters1, nt1, counters2, nt2);
 }
 
-cudaError_t launch_scatter_gather(const int32_t* ids, const int32_t* bases, int T, int E_l,
-                                  int local_offset, int R_cap, const void* hidden,
-                                  const float* hs_scale, int32_t* inv_row, int32_t* row_token,
-                                  uint8_t* act, float* act_scale, cudaStream_t st) {
-  const int nb = (T + kRouteTokensPerCta - 1) / kRouteTokensPerCta;
+cudaError_t launch_scatter(const int32_t* ids, const uint32_t* masks, const int32_t* bases, int T,
+                           int E_l, int local_offset, int32_t* inv_row, int32_t* row_token,
+                           cudaStream_t st) {
+  const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
-  scatter_gather_kernel<<<nb, 256, 0, st>>>(ids, bases, T, E_l, local_offset, R_cap,
-                                            static_cast<const uint8_t*>(hidden), hs_scale,
-                                            inv_row, row_token, act, act_scale);
-  return cudaGetLastError();
+  return launch_pdl(scatter_kernel, dim3(nb), dim3(kPermBlock * kTopK), 0, st, ids, masks, bases, T,
+                    E_l, local_offset, inv_row, row_token);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
                            void* out, float* out_f32, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  combine_kernel<<<T, 256, 0, st>>>(down, inv_row, w, T, static_cast<__nv_bfloat16*>(out),
-                                    out_f32);
-  return cudaGetLastError();
+  return launch_pdl(combine_kernel, dim3(T), dim3(256), 0, st, down, inv_row, w, T,
+                    static_cast<__nv_bfloat16*>(out), out_f32);
 }
 
 }  // namespace moe
