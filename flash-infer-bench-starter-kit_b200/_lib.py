@@ -59,7 +59,7 @@ EXPORTS = (
     "moe_fp8_ds_workspace_size", "moe_fp8_ds_workspace_layout", "moe_fp8_ds_run",
     "moe_fp8_ds_run_routed", "moe_fp8_ds_route", "moe_fp8_ds_read_device_error",
     "moe_fp8_ds_status_string", "moe_fp8_ds_launches_per_call", "moe_fp8_ds_set_tile_override",
-    "moe_fp8_ds_set_stage_events",
+    "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc",
 )
 
 _lib = None
@@ -88,6 +88,7 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_workspace_layout.argtypes = [I32, I32, ctypes.POINTER(MoeLayout)]
         lib.moe_fp8_ds_run.argtypes = [ctypes.POINTER(MoeArgs), P, U64, P]
         lib.moe_fp8_ds_run_routed.argtypes = [ctypes.POINTER(MoeArgs), P, U64, P]
+        lib.moe_fp8_ds_run_noalloc.argtypes = [ctypes.POINTER(MoeArgs), P]
         lib.moe_fp8_ds_route.argtypes = [P, P, I32, ctypes.c_float, P, P, P]
         lib.moe_fp8_ds_read_device_error.argtypes = [P, P, ctypes.POINTER(I32)]
         lib.moe_fp8_ds_status_string.argtypes = [ctypes.c_int]

@@ -231,6 +231,13 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
 }
 
 }  // namespace
+
+// Internal entry for other translation units of this library.
+int run_layer_with_workspace(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream,
+                             bool routed) {
+  return run_impl(a, ws, ws_bytes, stream, routed);
+}
+
 }  // namespace moe
 
 using namespace moe;

@@ -43,4 +43,8 @@ cudaError_t launch_scatter(const int32_t* ids, const uint32_t* masks, const int3
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
                            void* out, float* out_f32, cudaStream_t st);
 
+// Defined in api.cu: one full layer call on a caller-provided workspace.
+int run_layer_with_workspace(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream,
+                             bool routed);
+
 }  // namespace moe

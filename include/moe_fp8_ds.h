@@ -121,6 +121,19 @@ MOE_API int moe_fp8_ds_run(const moe_fp8_ds_args* args, void* workspace, uint64_
 MOE_API int moe_fp8_ds_run_routed(const moe_fp8_ds_args* args, void* workspace,
                           uint64_t workspace_bytes, void* stream);
 
+/* Allocation-free layer call, for callers that cannot allocate device
+ * memory where they call the layer (an external memory manager owns all
+ * allocations, or cudaMalloc is not allowed on the serving path).  No
+ * counterpart in the reference.  Same arguments and result as
+ * moe_fp8_ds_run, but the workspace is a 16 MiB array inside this library
+ * that every GPU loading the library keeps until the process exits; T is
+ * limited to 16 tokens (MOE_ERR_TOO_LARGE beyond).  The first call on a
+ * device looks up that array's device address, so make it before any stream
+ * capture.  All calls on a device share the array: calls that overlap on the
+ * GPU (different streams, or threads) race and must be serialised by the
+ * caller.  Device-side errors are not reported by this entry point.        */
+MOE_API int moe_fp8_ds_run_noalloc(const moe_fp8_ds_args* args, void* stream);
+
 /* Routing only: writes ids (ascending per token) and weights.              */
 MOE_API int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
                      float routed_scaling_factor, int32_t* topk_ids, float* topk_weights,
