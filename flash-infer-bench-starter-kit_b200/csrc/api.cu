@@ -72,7 +72,7 @@ int pick_bn(int T, int E_l) {
 
 struct Plan {
   moe_fp8_ds_layout pub;
-  int T, E_l, NB, R_cap, bn1, bn2, grid, max_mt1, max_mt2;
+  int T, E_l, NB, NB8, R_cap, bn1, bn2, grid, max_mt1, max_mt2;
   uint64_t tiles1, tiles2, sched, counters1, counters2, partials1, partials2;
 };
 
@@ -100,7 +100,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.topk_ids = take((uint64_t)T * kTopK * 4);
   P->pub.topk_weights = take((uint64_t)T * kTopK * 4);
   P->pub.inv_row = take((uint64_t)T * kTopK * 4);
-  P->pub.block_masks = take((uint64_t)P->NB * E_l * 4);
+  P->NB8 = (T + kRouteTokens - 1) / kRouteTokens;
+  P->pub.block_masks = take((uint64_t)P->NB8 * E_l);
   P->pub.block_bases = take((uint64_t)P->NB * E_l * 4);
   P->pub.seg_offsets = take((uint64_t)(E_l + 1) * 4);
   P->tiles1 = take((uint64_t)P->max_mt1 * 16);
@@ -109,6 +110,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->pub.row_token = take(R * 4);
+  P->pub.act = take(R * kHidden);
+  P->pub.act_scale = take(R * kHiddenBlocks * 4);
   P->pub.inter = take(2 * R * kInter);
   P->pub.inter_scale = take(R * kInterBlocks * 4);
   P->pub.down = take(R * kHidden * 4);
@@ -118,12 +121,16 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.row_capacity = P->R_cap;
 }
 
-bool encode_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows) {
-  cuuint64_t dims[2] = {inner, rows};
-  cuuint64_t strides[1] = {inner};          // bytes (1-byte elements)
-  cuuint32_t box[2] = {128, box_rows};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides,
+// 3D view of a K-major e4m3 matrix [rows, K]: x = byte inside a 128-wide K
+// block, y = row, z = K block; a box covers box_rows rows x kblocks K blocks,
+// landing as kblocks consecutive 128-byte-swizzled [box_rows x 128] tiles.
+bool encode_kmajor(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows,
+                   uint32_t kblocks) {
+  cuuint64_t dims[3] = {128, rows, K / 128};
+  cuuint64_t strides[2] = {K, 128};         // bytes (1-byte elements)
+  cuuint32_t box[3] = {128, box_rows, kblocks};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides,
                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
@@ -171,7 +178,9 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   int32_t* ids = routed ? const_cast<int32_t*>(a->topk_ids) : reinterpret_cast<int32_t*>(at(P.pub.topk_ids));
   float* wts = routed ? const_cast<float*>(a->topk_weights) : reinterpret_cast<float*>(at(P.pub.topk_weights));
   int32_t* inv = reinterpret_cast<int32_t*>(at(P.pub.inv_row));
-  uint32_t* masks = reinterpret_cast<uint32_t*>(at(P.pub.block_masks));
+  uint8_t* masks8 = at(P.pub.block_masks);
+  uint8_t* act = at(P.pub.act);
+  float* act_scale = reinterpret_cast<float*>(at(P.pub.act_scale));
   int32_t* bases = reinterpret_cast<int32_t*>(at(P.pub.block_bases));
   int32_t* seg = reinterpret_cast<int32_t*>(at(P.pub.seg_offsets));
   int4* tiles1 = reinterpret_cast<int4*>(at(P.tiles1));
@@ -186,28 +195,30 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
-  if (!encode_2d(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128) ||
-      !encode_2d(&tm_b1, a->hidden_states, kHidden, (uint64_t)T, 1) ||
-      !encode_2d(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128) ||
-      !encode_2d(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2)))
+  const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
+  if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
+      !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1, ks1) ||
+      !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
+      !encode_kmajor(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2), ks2))
     return MOE_ERR_INVALID_ARGUMENT;
 
   cudaError_t ce;
   mark_stage(0, s);
   ce = launch_route(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
-                    a->local_expert_offset, E_l, ids, wts, masks, err, s);
+                    a->local_expert_offset, E_l, ids, wts, masks8, err, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
   mark_stage(1, s);
-  ce = launch_scan(masks, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
+  ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
                    kInter / 128, cnt2, kHidden / 128, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
   mark_stage(2, s);
-  ce = launch_scatter(ids, masks, bases, T, E_l, a->local_expert_offset, inv, row_token, s);
+  ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
+                      a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   GemmParams g1{};
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
-  g1.b_scale = a->hidden_states_scale; g1.b_scale_stride = T; g1.row_token = row_token;
+  g1.b_scale = act_scale;
   g1.counters = cnt1; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
@@ -216,7 +227,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
 
   GemmParams g2{};
   g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale;
-  g2.b_scale = inter_scale; g2.b_scale_stride = P.R_cap; g2.row_token = nullptr;
+  g2.b_scale = inter_scale;
   g2.counters = cnt2; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);

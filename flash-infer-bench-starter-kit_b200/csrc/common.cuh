@@ -30,6 +30,8 @@ constexpr float kFp8Max = 448.0f;
 // Permutation block: tokens per routing CTA (one warp per token); the
 // per-block expert masks are 32-bit.
 constexpr int kPermBlock = 32;
+// Tokens routed per CTA (one warp each); four route CTAs make a permutation block.
+constexpr int kRouteTokens = 8;
 
 // A bounded wait gives up after this many nanoseconds and raises the
 // device error word; every kernel here finishes in well under a second.
@@ -137,6 +139,16 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// 3D tiled load: x = byte inside a 128-byte K block, y = row, z = K block.
+__device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
+                                            int32_t x, int32_t y, int32_t z, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
       : "memory");
 }
 

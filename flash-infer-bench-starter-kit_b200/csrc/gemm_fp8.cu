@@ -9,6 +9,8 @@
 // fills the tensor core's M dimension and the weight stream is the only large
 // operand.  Both operands are K-major e4m3 tiles loaded by TMA with 128-byte
 // swizzling; one tcgen05.mma of K=32 is issued four times per 128-wide K block.
+// The token operand of GEMM1 is the permuted activation the scatter kernel
+// gathered, so each token tile is one TMA box.
 //
 // Block scales: the fp32 128x128 weight scale is a scalar per (tile, K block),
 // the fp32 1x128 activation scale is per token column.  Because they are
@@ -27,6 +29,11 @@
 // each token, so one MMA of N = 2*BN yields both; the epilogue folds them as
 // (P_hi + P_lo/16) * s.
 //
+// K steps: one pipeline stage holds KS consecutive 128-wide K blocks, loaded
+// by one 3D TMA box per operand ({128 bytes, rows, KS blocks}), because the
+// TMA engine's cost is per box: fewer, larger boxes stream weights faster.
+// Each K block still gets its own TMEM partial and its own scale promotion.
+//
 // Scheduling: persistent, one CTA per SM, stream-K.  The work is the list of
 // (n-tile, token tile) units times K blocks; every CTA gets one contiguous
 // range of that iteration space.  A unit split between CTAs is finished by the
@@ -39,30 +46,35 @@
 
 namespace moe {
 
-template <int KIND, int BN, int STAGES, int NWG>
+template <int KIND, int BN, int STAGES, int NWG, int KS>
 struct GemmCfg {
-  static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles per stage
+  static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles per K block
   static constexpr int MMA_N = KIND == 1 ? BN : 2 * BN;     // token-operand rows
   static constexpr int KB = KIND == 1 ? kHiddenBlocks : kInterBlocks;
+  static constexpr int KSTEPS = KB / KS;                    // pipeline iterations per unit
   static constexpr int NT = KIND == 1 ? kInter / 128 : kHidden / 128;   // n-tiles per expert
   static constexpr int W_ROWS = KIND == 1 ? kGemm1Out : kHidden;        // weight rows per expert
   static constexpr int W_TILE = 128 * 128;
   static constexpr int B_TILE = MMA_N * 128;
-  static constexpr int STAGE = NW * W_TILE + B_TILE;
-  static constexpr int NBUF = 4 * NW * MMA_N <= 512 ? 4 : 2;   // TMEM partial buffers
-  static constexpr int TMEM_USED = NBUF * NW * MMA_N;
+  static constexpr int STAGE = KS * (NW * W_TILE + B_TILE);
+  static constexpr int BUF_COLS = KS * NW * MMA_N;          // TMEM columns of one partial buffer
+  static constexpr int NBUF = 4 * BUF_COLS <= 512 ? 4 : 2;
+  static constexpr int TMEM_USED = NBUF * BUF_COLS;
   static constexpr int TMEM_COLS = TMEM_USED <= 32 ? 32 : TMEM_USED <= 64 ? 64
                                  : TMEM_USED <= 128 ? 128 : TMEM_USED <= 256 ? 256 : 512;
   static constexpr int NEPI = 128 * NWG;
   static constexpr int THREADS = 64 + NEPI;
   static constexpr int CPW = BN / NWG;                      // token columns per warpgroup
-  static constexpr int SLOT = BN + NW;                      // per-iteration scales: tokens + weight
-  static constexpr int RING = 3;                            // scale slots (prefetch distance 2)
-  static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4 + BN * 4;
+  static constexpr int SUB = BN + NW;                       // scales of one K block
+  static constexpr int SLOT = KS * SUB;                     // scales of one iteration
+  static constexpr int RING = 3;                            // slots (prefetch distance 2)
+  static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4;
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
-  static_assert(TMEM_USED <= 512, "TMEM budget");
+  static_assert(KB % KS == 0, "K steps");
+  static_assert(TMEM_USED <= 512 && NBUF >= 2, "TMEM budget");
   static_assert(CPW % 16 == 0 || (KIND == 2 && CPW % 8 == 0), "column chunking");
   static_assert(MMA_N % 16 == 0 && MMA_N <= 256, "MMA N");
+  static_assert(SLOT <= NEPI, "one scale per epilogue thread");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -70,22 +82,22 @@ struct Schedule {
   int n_mt, units, total, L, it0, it1;
 };
 
-__device__ __forceinline__ Schedule make_schedule(int n_mt, int NT, int KB) {
+__device__ __forceinline__ Schedule make_schedule(int n_mt, int NT, int KSTEPS) {
   Schedule s;
   s.n_mt = n_mt;
   s.units = n_mt * NT;
-  s.total = s.units * KB;
+  s.total = s.units * KSTEPS;
   s.L = (s.total + gridDim.x - 1) / gridDim.x;
   s.it0 = min(s.total, (int)blockIdx.x * s.L);
   s.it1 = min(s.total, s.it0 + s.L);
   return s;
 }
 
-template <int KIND, int BN, int STAGES, int NWG>
-__global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG>::THREADS, 1)
+template <int KIND, int BN, int STAGES, int NWG, int KS>
+__global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG, KS>::THREADS, 1)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
                 const GemmParams p) {
-  using C = GemmCfg<KIND, BN, STAGES, NWG>;
+  using C = GemmCfg<KIND, BN, STAGES, NWG, KS>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for 128-byte-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -97,17 +109,16 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   uint64_t* drain = tempty + C::NBUF;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  int* last_flag = const_cast<int*>(abort_flag) + 1;     // [NWG]
+  int* last_flag = const_cast<int*>(abort_flag) + 1;
   float* sring = reinterpret_cast<float*>(aux + 2048);     // [RING][SLOT] scales per iteration
   float* samax = sring + C::RING * C::SLOT;                // [NWG][4][CPW]
-  int* s_tok = reinterpret_cast<int*>(samax + NWG * 4 * C::CPW);   // [BN] GEMM1 token rows
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   griddep_wait();                   // routing/permutation (or GEMM1) results are visible
   griddep_launch_dependents();
-  const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KB);
+  const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KSTEPS);
   if (sch.it0 >= sch.it1) return;   // uniform: this CTA has no work
   const int n_iter = sch.it1 - sch.it0;
 
@@ -127,54 +138,36 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    // Lane 0 issues the TMA copies; for GEMM1 the whole warp first stages the
-    // tile's source-token ids, which the row gathers (tile::gather4) read.
-    const uint64_t pol_w = l2_policy_evict_first();
-    const uint64_t pol_b = l2_policy_evict_last();
-    int issued = 0;
-    bool ok = true;
-    for (int i = 0; i < n_iter; ++i) {
-      const int it = sch.it0 + i;
-      const int u = it / C::KB, kb = it % C::KB;
-      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
-      const int4 tile = p.tiles[mt];
-      if (KIND == 1 && (i == 0 || kb == 0)) {
-        for (int j = lane; j < BN; j += 32)
-          s_tok[j] = __ldg(p.row_token + tile.y + (j < tile.z ? j : 0));
-        __syncwarp();
+    if (elect_one_lane()) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_b = l2_policy_evict_last();
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < n_iter; ++i) {
+        const int it = sch.it0 + i;
+        const int u = it / C::KSTEPS, ks = it % C::KSTEPS;
+        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+        const int4 tile = p.tiles[mt];
+        const int s = i % STAGES;
+        if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
+        uint8_t* st = smem + s * C::STAGE;
+        const int z = ks * KS;
+        const int wrow = tile.x * C::W_ROWS + nt * 128;
+        tma_load_3d(&tm_w, &full[s], st, 0, wrow, z, pol_w);
+        if (KIND == 1) tma_load_3d(&tm_w, &full[s], st + KS * C::W_TILE, 0, wrow + kInter, z, pol_w);
+        tma_load_3d(&tm_b, &full[s], st + C::NW * KS * C::W_TILE, 0,
+                    KIND == 1 ? tile.y : 2 * tile.y, z, pol_b);
+        ++issued;
       }
-      const int s = i % STAGES;
-      if (lane == 0) {
-        ok = mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag);
-        if (ok) {
-          mbar_arrive_expect_tx(&full[s], C::STAGE);
-          uint8_t* st = smem + s * C::STAGE;
-          const int x = kb * 128;
-          const int wrow = tile.x * C::W_ROWS + nt * 128;
-          tma_load_2d(&tm_w, &full[s], st, x, wrow, pol_w);
-          if (KIND == 1) {
-            tma_load_2d(&tm_w, &full[s], st + C::W_TILE, x, wrow + kInter, pol_w);
-            uint8_t* dst = st + C::NW * C::W_TILE;
-#pragma unroll
-            for (int g = 0; g < BN / 4; ++g)
-              tma_gather4(&tm_b, &full[s], dst + g * 512, x, s_tok[4 * g], s_tok[4 * g + 1],
-                          s_tok[4 * g + 2], s_tok[4 * g + 3], pol_b);
-          } else {
-            tma_load_2d(&tm_b, &full[s], st + C::NW * C::W_TILE, x, 2 * tile.y, pol_b);
-          }
-          ++issued;
+      if (!ok) {
+        raise_error(p.err, kDevTimeoutProducer);
+        // Let copies already in flight land before the CTA exits.
+        for (int i = max(0, issued - STAGES); i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+                 globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
         }
-      }
-      ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
-      if (!ok) break;
-    }
-    if (!ok && lane == 0) {
-      raise_error(p.err, kDevTimeoutProducer);
-      // Let copies already in flight land before the CTA exits.
-      for (int i = max(0, issued - STAGES); i < issued; ++i) {
-        const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
-               globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
       }
     }
   } else if (warp == 1) {
@@ -189,14 +182,17 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (!mbar_wait_bounded(&tempty[b], ((i / C::NBUF) & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = smem_base + s * C::STAGE;
-        const uint64_t bdesc = make_sdesc_sw128(st + C::NW * C::W_TILE);
 #pragma unroll
-        for (int w = 0; w < C::NW; ++w) {
-          const uint64_t adesc = make_sdesc_sw128(st + w * C::W_TILE);
-          const uint32_t d = tmem_base + (uint32_t)(b * C::NW * C::MMA_N + w * C::MMA_N);
+        for (int kk = 0; kk < KS; ++kk) {
+          const uint64_t bdesc = make_sdesc_sw128(st + C::NW * KS * C::W_TILE + kk * C::B_TILE);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)   // 4 x K=32 per 128-byte K block; +32 B = +2 in addr>>4
-            tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+          for (int w = 0; w < C::NW; ++w) {
+            const uint64_t adesc = make_sdesc_sw128(st + (w * KS + kk) * C::W_TILE);
+            const uint32_t d = tmem_base + (uint32_t)(b * C::BUF_COLS + (kk * C::NW + w) * C::MMA_N);
+#pragma unroll
+            for (int k = 0; k < 4; ++k)   // 4 x K=32 per 128-byte K block; +32 B = +2 in addr>>4
+              tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc, k > 0 ? 1u : 0u);
+          }
         }
         tc_commit(&empty[s]);
         tc_commit(&tfull[b]);
@@ -217,81 +213,85 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
 
     float acc[C::NW][C::CPW];
-    int seg_kb0 = 0;
+    int seg_k0 = 0;
     int4 tile = make_int4(0, 0, 0, 0);
 
-    // Scales of iteration i live in ring slot i % RING: [0, BN) token-column
-    // scales, [BN, BN+NW) weight-block scales.  Thread et < BN+NW loads its
-    // entry two iterations ahead, so the loads never sit on the critical path.
+    // Scales of iteration i live in ring slot i % RING; per K block kk the
+    // entries [kk*SUB, kk*SUB+BN) are token-column scales and the next NW the
+    // weight-block scales.  Thread et < SLOT loads its entry two iterations
+    // ahead, so the loads never sit on the critical path.
+    const bool loader = et < C::SLOT;
+    const int my_kk = et / C::SUB, my_e = et % C::SUB;
     int pf_unit = -1, pf_col = -1, pf_e = 0, pf_nt = 0;
     auto fetch = [&](int i_t) -> float {
       const int it_t = sch.it0 + i_t;
-      const int u_t = it_t / C::KB, kb_t = it_t % C::KB;
+      const int u_t = it_t / C::KSTEPS;
+      const int kb_t = (it_t % C::KSTEPS) * KS + my_kk;
       if (u_t != pf_unit) {
         pf_unit = u_t;
         const int4 tl = p.tiles[u_t % sch.n_mt];
         pf_e = tl.x;
         pf_nt = u_t / sch.n_mt;
-        pf_col = -1;
-        if (et < BN && et < tl.z) pf_col = KIND == 1 ? __ldg(p.row_token + tl.y + et) : tl.y + et;
+        pf_col = (my_e < BN && my_e < tl.z) ? tl.y + my_e : -1;
       }
-      if (et < BN) return pf_col >= 0 ? __ldg(p.b_scale + (size_t)kb_t * p.b_scale_stride + pf_col) : 0.f;
-      const int w = et - BN;
+      if (my_e < BN) return pf_col >= 0 ? __ldg(p.b_scale + (size_t)kb_t * p.R_cap + pf_col) : 0.f;
+      const int w = my_e - BN;
       const int nb = KIND == 1 ? pf_nt + w * (kInter / 128) : pf_nt;
       return __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
     };
-    const bool loader = et < C::SLOT;
     for (int i_t = 0; i_t < 2 && i_t < n_iter; ++i_t)
       if (loader) sring[i_t * C::SLOT + et] = fetch(i_t);
     named_bar_sync(1, C::NEPI);
 
     for (int i = 0; i < n_iter; ++i) {
       const int it = sch.it0 + i;
-      const int u = it / C::KB, kb = it % C::KB;
+      const int u = it / C::KSTEPS, ks = it % C::KSTEPS;
       const int nt = u / sch.n_mt, mt = u % sch.n_mt;
       const int b = i % C::NBUF;
-      if (i == 0 || kb == 0) {
+      if (i == 0 || ks == 0) {
         tile = p.tiles[mt];
-        seg_kb0 = kb;
+        seg_k0 = ks;
 #pragma unroll
         for (int w = 0; w < C::NW; ++w)
 #pragma unroll
           for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
       }
       const float pre = (loader && i + 2 < n_iter) ? fetch(i + 2) : 0.f;
-      const float* sb = sring + (i % C::RING) * C::SLOT;
-      float wsc[C::NW];
-#pragma unroll
-      for (int w = 0; w < C::NW; ++w) wsc[w] = sb[BN + w];
+      const float* sl = sring + (i % C::RING) * C::SLOT;
       const bool got = mbar_wait_bounded(&tfull[b], (i / C::NBUF) & 1, abort_flag);
       if (got) {
         tc_fence_after();
 #pragma unroll
-        for (int w = 0; w < C::NW; ++w) {
-          const uint32_t col0 = (uint32_t)(b * C::NW * C::MMA_N + w * C::MMA_N);
-          if (KIND == 1) {
+        for (int kk = 0; kk < KS; ++kk) {
+          const float* sb = sl + kk * C::SUB;
 #pragma unroll
-            for (int c = 0; c < C::CPW / 16; ++c) {
-              float v[16];
-              tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v);
-              tmem_ld_wait();
+          for (int w = 0; w < C::NW; ++w) {
+            const float wsc = sb[BN + w];
+            const uint32_t col0 = (uint32_t)(b * C::BUF_COLS + (kk * C::NW + w) * C::MMA_N);
+            if (KIND == 1) {
 #pragma unroll
-              for (int x = 0; x < 16; ++x) {
-                const int jj = c * 16 + x;
-                acc[w][jj] = fmaf(v[x], wsc[w] * sb[j0 + jj], acc[w][jj]);
+              for (int c = 0; c < C::CPW / 16; ++c) {
+                float v[16];
+                tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v);
+                tmem_ld_wait();
+#pragma unroll
+                for (int x = 0; x < 16; ++x) {
+                  const int jj = c * 16 + x;
+                  acc[w][jj] = fmaf(v[x], wsc * sb[j0 + jj], acc[w][jj]);
+                }
               }
-            }
-          } else {
+            } else {
 #pragma unroll
-            for (int c = 0; c < C::CPW / 8; ++c) {
-              float v[16];
-              tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v);
-              tmem_ld_wait();
+              for (int c = 0; c < C::CPW / 8; ++c) {
+                float v[16];
+                tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v);
+                tmem_ld_wait();
 #pragma unroll
-              for (int x = 0; x < 8; ++x) {
-                const int jj = c * 8 + x;
-                const float pv = fmaf(v[2 * x + 1], 0.0625f, v[2 * x]);
-                acc[w][jj] = fmaf(pv, wsc[w] * sb[j0 + jj], acc[w][jj]);
+                for (int x = 0; x < 8; ++x) {
+                  const int jj = c * 8 + x;
+                  const float pv = fmaf(v[2 * x + 1], 0.0625f, v[2 * x]);
+                  acc[w][jj] = fmaf(pv, wsc * sb[j0 + jj], acc[w][jj]);
+                }
               }
             }
           }
@@ -304,13 +304,13 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       named_bar_sync(1, C::NEPI);
       if (*abort_flag) break;
 
-      const bool seg_last = (kb == C::KB - 1) || (it == sch.it1 - 1);
+      const bool seg_last = (ks == C::KSTEPS - 1) || (it == sch.it1 - 1);
       if (!seg_last) continue;
 
       // ---------------- end of this CTA's share of unit u
-      if (!(seg_kb0 == 0 && kb == C::KB - 1)) {
+      if (!(seg_k0 == 0 && ks == C::KSTEPS - 1)) {
         // stream-K: publish the partial, the last contributor finishes the unit
-        const int first_unit = sch.it0 / C::KB;
+        const int first_unit = sch.it0 / C::KSTEPS;
         const int slot = (u == first_unit) ? 0 : 1;
         float* mine = p.partials + ((size_t)(blockIdx.x * 2 + slot) * C::NW) * BN * 128;
 #pragma unroll
@@ -320,8 +320,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             __stcg(mine + ((size_t)w * BN + j0 + jj) * 128 + f, acc[w][jj]);
         __threadfence();
         named_bar_sync(1, C::NEPI);
-        const int c_lo = (u * C::KB) / sch.L;
-        const int c_hi = ((u + 1) * C::KB - 1) / sch.L;
+        const int c_lo = (u * C::KSTEPS) / sch.L;
+        const int c_hi = ((u + 1) * C::KSTEPS - 1) / sch.L;
         if (et == 0) {
           const int old = atomicAdd(p.counters + u, 1);
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
@@ -334,7 +334,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
           for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
         for (int c = c_lo; c <= c_hi; ++c) {
-          const int cslot = (u == (c * sch.L) / C::KB) ? 0 : 1;
+          const int cslot = (u == (c * sch.L) / C::KSTEPS) ? 0 : 1;
           const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
 #pragma unroll
           for (int w = 0; w < C::NW; ++w)
@@ -343,7 +343,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
               acc[w][jj] += __ldcg(src + ((size_t)w * BN + j0 + jj) * 128 + f);
         }
       }
-
       if (KIND == 1) {
         // SwiGLU: c = silu(X2) * X1, X1 = acc[0], X2 = acc[1]
         float* my_amax = samax + (wg * 4 + q) * C::CPW;
@@ -399,75 +398,64 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 }
 
 // --------------------------------------------------------------------------
-// Host-side dispatch
+// Host-side dispatch: (kind, BN) -> stages, warpgroups, K blocks per stage.
 // --------------------------------------------------------------------------
 template <int KIND, int BN> struct Pick;
-template <> struct Pick<1, 16> { using C = GemmCfg<1, 16, 6, 1>; static constexpr int S = 6, W = 1; };
-template <> struct Pick<1, 32> { using C = GemmCfg<1, 32, 6, 1>; static constexpr int S = 6, W = 1; };
-template <> struct Pick<1, 64> { using C = GemmCfg<1, 64, 5, 1>; static constexpr int S = 5, W = 1; };
-template <> struct Pick<1, 128> { using C = GemmCfg<1, 128, 4, 2>; static constexpr int S = 4, W = 2; };
-template <> struct Pick<2, 16> { using C = GemmCfg<2, 16, 10, 1>; static constexpr int S = 10, W = 1; };
-template <> struct Pick<2, 32> { using C = GemmCfg<2, 32, 8, 1>; static constexpr int S = 8, W = 1; };
-template <> struct Pick<2, 64> { using C = GemmCfg<2, 64, 6, 1>; static constexpr int S = 6, W = 1; };
-template <> struct Pick<2, 128> { using C = GemmCfg<2, 128, 4, 2>; static constexpr int S = 4, W = 2; };
+template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2; };
+template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2; };
+template <> struct Pick<1, 64> { static constexpr int S = 5, W = 1, K = 1; };
+template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1; };
+template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2; };
+template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2; };
+template <> struct Pick<2, 64> { static constexpr int S = 6, W = 1, K = 1; };
+template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1; };
+
+template <int KIND, int BN>
+using CfgOf = GemmCfg<KIND, BN, Pick<KIND, BN>::S, Pick<KIND, BN>::W, Pick<KIND, BN>::K>;
 
 template <int KIND, int BN>
 static cudaError_t launch_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
                               int grid, cudaStream_t st) {
   using P = Pick<KIND, BN>;
-  using C = typename P::C;
-  auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W>;
+  using C = CfgOf<KIND, BN>;
+  auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W, P::K>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
 }
 
-template <int KIND, int BN>
-static size_t partials_one(int grid) {
-  using C = typename Pick<KIND, BN>::C;
-  return (size_t)grid * 2 * C::NW * BN * 128 * sizeof(float);
-}
+#define MOE_GEMM_CASES(X) X(1, 16) X(1, 32) X(1, 64) X(1, 128) X(2, 16) X(2, 32) X(2, 64) X(2, 128)
 
 size_t gemm_partials_bytes(int kind, int bn, int grid) {
-  switch (kind * 1000 + bn) {
-    case 1016: return partials_one<1, 16>(grid);
-    case 1032: return partials_one<1, 32>(grid);
-    case 1064: return partials_one<1, 64>(grid);
-    case 1128: return partials_one<1, 128>(grid);
-    case 2016: return partials_one<2, 16>(grid);
-    case 2032: return partials_one<2, 32>(grid);
-    case 2064: return partials_one<2, 64>(grid);
-    case 2128: return partials_one<2, 128>(grid);
-  }
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return (size_t)grid * 2 * CfgOf<KD, BB>::NW * BB * 128 * sizeof(float);
+  MOE_GEMM_CASES(X)
+#undef X
+  return 0;
+}
+
+int gemm_k_per_stage(int kind, int bn) {
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return Pick<KD, BB>::K;
+  MOE_GEMM_CASES(X)
+#undef X
   return 0;
 }
 
 int gemm_threads(int kind, int bn) {
-  switch (kind * 1000 + bn) {
-    case 1016: return Pick<1, 16>::C::THREADS;
-    case 1032: return Pick<1, 32>::C::THREADS;
-    case 1064: return Pick<1, 64>::C::THREADS;
-    case 1128: return Pick<1, 128>::C::THREADS;
-    case 2016: return Pick<2, 16>::C::THREADS;
-    case 2032: return Pick<2, 32>::C::THREADS;
-    case 2064: return Pick<2, 64>::C::THREADS;
-    case 2128: return Pick<2, 128>::C::THREADS;
-  }
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return CfgOf<KD, BB>::THREADS;
+  MOE_GEMM_CASES(X)
+#undef X
   return 0;
 }
 
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st) {
-  switch (kind * 1000 + bn) {
-    case 1016: return launch_one<1, 16>(tm_w, tm_b, p, grid, st);
-    case 1032: return launch_one<1, 32>(tm_w, tm_b, p, grid, st);
-    case 1064: return launch_one<1, 64>(tm_w, tm_b, p, grid, st);
-    case 1128: return launch_one<1, 128>(tm_w, tm_b, p, grid, st);
-    case 2016: return launch_one<2, 16>(tm_w, tm_b, p, grid, st);
-    case 2032: return launch_one<2, 32>(tm_w, tm_b, p, grid, st);
-    case 2064: return launch_one<2, 64>(tm_w, tm_b, p, grid, st);
-    case 2128: return launch_one<2, 128>(tm_w, tm_b, p, grid, st);
-  }
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return launch_one<KD, BB>(tm_w, tm_b, p, grid, st);
+  MOE_GEMM_CASES(X)
+#undef X
   return cudaErrorInvalidValue;
 }
 

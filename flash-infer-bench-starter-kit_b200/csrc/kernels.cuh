@@ -10,9 +10,7 @@ struct GemmParams {
   const int4* tiles;          // (local expert, first row, rows, 0) per token tile
   const int32_t* sched;       // sched[0] = #tiles for GEMM1, sched[1] = #tiles for GEMM2
   const float* w_scale;       // GEMM1: [E_l, 32, 56]; GEMM2: [E_l, 56, 16]
-  const float* b_scale;       // GEMM1: hidden_states_scale [56, T]; GEMM2: inter_scale [16, R_cap]
-  int b_scale_stride;         // T for GEMM1, R_cap for GEMM2
-  const int32_t* row_token;   // GEMM1: source token of each permuted row
+  const float* b_scale;       // GEMM1: act_scale [56, R_cap]; GEMM2: inter_scale [16, R_cap]
   int32_t* counters;          // stream-K arrival counters, one per output tile
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048]
@@ -28,18 +26,20 @@ constexpr int kBnConfigs[kNumBnConfigs] = {16, 32, 64, 128};
 
 size_t gemm_partials_bytes(int kind, int bn, int grid);
 int gemm_threads(int kind, int bn);
+int gemm_k_per_stage(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st);
 
 cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
                          float scaling, int local_offset, int E_l, int32_t* ids, float* w,
-                         uint32_t* masks, int* err, cudaStream_t st);
-cudaError_t launch_scan(const uint32_t* masks, int32_t* bases, int NB, int E_l, int32_t* seg,
+                         uint8_t* masks8, int* err, cudaStream_t st);
+cudaError_t launch_scan(const uint8_t* masks8, int NB8, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
                         int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st);
-cudaError_t launch_scatter(const int32_t* ids, const uint32_t* masks, const int32_t* bases, int T,
-                           int E_l, int local_offset, int32_t* inv_row, int32_t* row_token,
-                           cudaStream_t st);
+cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8, const int32_t* bases, int T,
+                           int E_l, int local_offset, int R_cap, const void* hidden,
+                           const float* hs_scale, int32_t* inv_row, int32_t* row_token,
+                           uint8_t* act, float* act_scale, cudaStream_t st);
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
                            void* out, float* out_f32, cudaStream_t st);
 

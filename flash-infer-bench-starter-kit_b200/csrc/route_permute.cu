@@ -27,16 +27,17 @@ namespace moe {
 // accumulators, lanes summed last), so weights match the reference's own
 // fp32 arithmetic.  Ties in any top-k go to the lower index.
 //
-// masks[b][e] has bit w set when token 32b+w picked local expert e; the
-// scan turns popcounts into row offsets, the scatter turns masked
-// popcounts into each token's rank inside its expert (ascending tokens).
+// One CTA routes kRouteTokens tokens and writes the byte masks8[g][e], bit
+// w set when token 8g+w picked local expert e.  Four consecutive bytes form
+// the 32-token permutation-block mask the scan turns into row offsets and
+// the scatter into each token's rank inside its expert (ascending tokens).
 // --------------------------------------------------------------------------
 template <bool kFromIds>
-__global__ void __launch_bounds__(kPermBlock * 32)
+__global__ void __launch_bounds__(kRouteTokens * 32)
 route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias,
              int T, float scaling, int local_offset, int E_l,
              int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
-             uint32_t* __restrict__ masks, int* __restrict__ err) {
+             uint8_t* __restrict__ masks8, int* __restrict__ err) {
   __shared__ uint32_t s_mask[kExpertsGlobal];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -45,7 +46,7 @@ route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
   __syncthreads();
 
-  const int t = blockIdx.x * kPermBlock + warp;
+  const int t = blockIdx.x * kRouteTokens + warp;
   if (t < T) {
     int my_id = -1;  // lane k < 8 ends up holding the k-th id (ascending)
     if constexpr (!kFromIds) {
@@ -166,9 +167,21 @@ route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     }
   }
   __syncthreads();
-  if (masks)
+  if (masks8)
     for (int e = threadIdx.x; e < E_l; e += blockDim.x)
-      masks[(size_t)blockIdx.x * E_l + e] = s_mask[e];
+      masks8[(size_t)blockIdx.x * E_l + e] = static_cast<uint8_t>(s_mask[e]);
+}
+
+// 32-token block mask of block b for expert e from the four byte masks.
+__device__ __forceinline__ uint32_t block_mask(const uint8_t* __restrict__ masks8, int NB8, int E_l,
+                                               int b, int e) {
+  uint32_t m = 0;
+#pragma unroll
+  for (int q = 0; q < kPermBlock / kRouteTokens; ++q) {
+    const int g = b * (kPermBlock / kRouteTokens) + q;
+    if (g < NB8) m |= (uint32_t)masks8[(size_t)g * E_l + e] << (q * kRouteTokens);
+  }
+  return m;
 }
 
 // --------------------------------------------------------------------------
@@ -209,7 +222,7 @@ __device__ void warp0_scan_inplace(int* v, int n, int* total_out) {
 }
 
 __global__ void __launch_bounds__(1024)
-scan_kernel(const uint32_t* __restrict__ masks, int32_t* __restrict__ bases, int NB, int E_l,
+scan_kernel(const uint8_t* __restrict__ masks8, int NB8, int32_t* __restrict__ bases, int NB, int E_l,
             int32_t* __restrict__ seg_out,
             int bn1, int bn2, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
             int32_t* __restrict__ sched, int32_t* __restrict__ counters1, int nt1,
@@ -230,7 +243,7 @@ scan_kernel(const uint32_t* __restrict__ masks, int32_t* __restrict__ bases, int
     int run = 0;
     for (int b0 = 0; b0 < NB; b0 += 32) {
       int b = b0 + lane;
-      int v = b < NB ? __popc(masks[(size_t)b * E_l + e]) : 0;
+      int v = b < NB ? __popc(block_mask(masks8, NB8, E_l, b, e)) : 0;
       int tot;
       int ex = warp_exclusive_scan(v, lane, &tot);
       if (b < NB) bases[(size_t)b * E_l + e] = run + ex;   // relative to segment start
@@ -281,28 +294,62 @@ scan_kernel(const uint32_t* __restrict__ masks, int32_t* __restrict__ bases, int
 }
 
 // --------------------------------------------------------------------------
-// Scatter: rows of local expert e are its tokens in ascending order; the rank
-// of token 32b+w inside expert e is popc(masks[b][e] & ((1<<w)-1)).
-// Writes inv_row[t,k] (row or -1) and row_token[row].
+// Scatter + gather: rows of local expert e are its tokens in ascending order;
+// the rank of token 32b+w inside expert e is popc(masks[b][e] & ((1<<w)-1)).
+// CTA (b, c) handles the 32 tokens of block b and copies the 256-byte column
+// chunk c (two 128-wide K blocks) of each of their local rows into the
+// permuted activation act[R_cap, 7168], with the two matching scales; chunk
+// 0 also writes inv_row[t,k] (row or -1) and row_token[row].
 // --------------------------------------------------------------------------
+constexpr int kGatherChunk = 256;                          // bytes per CTA column chunk
+constexpr int kGatherChunks = kHidden / kGatherChunk;      // 28
+
 __global__ void __launch_bounds__(kPermBlock * kTopK)
-scatter_kernel(const int32_t* __restrict__ topk_ids, const uint32_t* __restrict__ masks,
-               const int32_t* __restrict__ bases, int T, int E_l, int local_offset,
-               int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token) {
+scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__ masks8, int NB8,
+               const int32_t* __restrict__ bases, int T, int E_l, int local_offset, int R_cap,
+               const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
+               int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
+               uint8_t* __restrict__ act, float* __restrict__ act_scale) {
+  __shared__ int s_row[kPermBlock * kTopK];
   griddep_wait();
   griddep_launch_dependents();
   const int i = blockIdx.x * kPermBlock * kTopK + threadIdx.x;   // (t, k) pair
   const int t = i / kTopK;
-  if (t >= T) return;
-  const int le = topk_ids[i] - local_offset;
   int row = -1;
-  if (le >= 0 && le < E_l) {
-    const int w = t - blockIdx.x * kPermBlock;
-    const size_t be = (size_t)blockIdx.x * E_l + le;
-    row = bases[be] + __popc(masks[be] & ((1u << w) - 1u));
-    row_token[row] = t;
+  if (t < T) {
+    const int le = topk_ids[i] - local_offset;
+    if (le >= 0 && le < E_l) {
+      const int w = t - blockIdx.x * kPermBlock;
+      const size_t be = (size_t)blockIdx.x * E_l + le;
+      row = bases[be] + __popc(block_mask(masks8, NB8, E_l, blockIdx.x, le) & ((1u << w) - 1u));
+    }
+    if (blockIdx.y == 0) {
+      inv_row[i] = row;
+      if (row >= 0) row_token[row] = t;
+    }
   }
-  inv_row[i] = row;
+  s_row[threadIdx.x] = row;
+  __syncthreads();
+  // copy: 16-byte vectors, (pair, vector) flattened over the CTA
+  constexpr int kVec = kGatherChunk / 16;
+  const size_t col = (size_t)blockIdx.y * kGatherChunk;
+  for (int v = threadIdx.x; v < kPermBlock * kTopK * kVec; v += blockDim.x) {
+    const int pr = v / kVec;
+    const int r = s_row[pr];
+    if (r < 0) continue;
+    const int tok = blockIdx.x * kPermBlock + pr / kTopK;
+    const int off = (v % kVec) * 16;
+    *reinterpret_cast<uint4*>(act + (size_t)r * kHidden + col + off) =
+        __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)tok * kHidden + col + off));
+  }
+  const int r = s_row[threadIdx.x];
+  if (r >= 0) {
+    const int tok = t;
+    const int kb0 = blockIdx.y * (kGatherChunk / kBlock);
+#pragma unroll
+    for (int q = 0; q < kGatherChunk / kBlock; ++q)
+      act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + tok);
+  }
 }
 
 // --------------------------------------------------------------------------
@@ -323,7 +370,7 @@ combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_r
     s_w[threadIdx.x] = topk_w[(size_t)t * kTopK + threadIdx.x];
   }
   __syncthreads();
-  for (int v = threadIdx.x; v < kHidden / 4; v += blockDim.x) {
+  for (int v = blockIdx.y * blockDim.x + threadIdx.x; v < kHidden / 4; v += blockDim.x * gridDim.y) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int k = 0; k < kTopK; ++k) {
@@ -355,37 +402,39 @@ combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_r
 // --------------------------------------------------------------------------
 cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
                          float scaling, int local_offset, int E_l, int32_t* ids, float* w,
-                         uint32_t* masks, int* err, cudaStream_t st) {
-  const int nb = (T + kPermBlock - 1) / kPermBlock;
+                         uint8_t* masks8, int* err, cudaStream_t st) {
+  const int nb = (T + kRouteTokens - 1) / kRouteTokens;
   if (nb == 0) return cudaSuccess;
   const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(bias);
   if (from_ids)
-    return launch_pdl(route_kernel<true>, dim3(nb), dim3(kPermBlock * 32), 0, st, logits, b, T,
-                      scaling, local_offset, E_l, ids, w, masks, err);
-  return launch_pdl(route_kernel<false>, dim3(nb), dim3(kPermBlock * 32), 0, st, logits, b, T,
-                    scaling, local_offset, E_l, ids, w, masks, err);
+    return launch_pdl(route_kernel<true>, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits, b, T,
+                      scaling, local_offset, E_l, ids, w, masks8, err);
+  return launch_pdl(route_kernel<false>, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits, b, T,
+                    scaling, local_offset, E_l, ids, w, masks8, err);
 }
 
-cudaError_t launch_scan(const uint32_t* masks, int32_t* bases, int NB, int E_l, int32_t* seg,
+cudaError_t launch_scan(const uint8_t* masks8, int NB8, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
                         int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st) {
-  return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks, bases, NB, E_l, seg, bn1, bn2,
+  return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks8, NB8, bases, NB, E_l, seg, bn1, bn2,
                     tiles1, tiles2, sched, counters1, nt1, counters2, nt2);
 }
 
-cudaError_t launch_scatter(const int32_t* ids, const uint32_t* masks, const int32_t* bases, int T,
-                           int E_l, int local_offset, int32_t* inv_row, int32_t* row_token,
-                           cudaStream_t st) {
+cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8, const int32_t* bases, int T,
+                           int E_l, int local_offset, int R_cap, const void* hidden,
+                           const float* hs_scale, int32_t* inv_row, int32_t* row_token,
+                           uint8_t* act, float* act_scale, cudaStream_t st) {
   const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
-  return launch_pdl(scatter_kernel, dim3(nb), dim3(kPermBlock * kTopK), 0, st, ids, masks, bases, T,
-                    E_l, local_offset, inv_row, row_token);
+  return launch_pdl(scatter_kernel, dim3(nb, kGatherChunks), dim3(kPermBlock * kTopK), 0, st, ids,
+                    masks8, NB8, bases, T, E_l, local_offset, R_cap, static_cast<const uint8_t*>(hidden),
+                    hs_scale, inv_row, row_token, act, act_scale);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
                            void* out, float* out_f32, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
-  return launch_pdl(combine_kernel, dim3(T), dim3(256), 0, st, down, inv_row, w, T,
+  return launch_pdl(combine_kernel, dim3(T, (kHidden / 4 + 255) / 256), dim3(256), 0, st, down, inv_row, w, T,
                     static_cast<__nv_bfloat16*>(out), out_f32);
 }
 

@@ -90,11 +90,13 @@ typedef struct moe_fp8_ds_layout {
   uint64_t inv_row;         /* int32 [T, 8]   permuted row of (t,k) or -1         */
   uint64_t seg_offsets;     /* int32 [E_l+1]  rows of local expert e              */
   uint64_t row_token;       /* int32 [R_cap]  source token of each permuted row   */
-  uint64_t block_masks;     /* uint32 [ceil(T/32), E_l] bit w: token 32b+w picked e */
+  uint64_t block_masks;     /* uint8 [ceil(T/8), E_l]  bit w: token 8g+w picked e  */
   uint64_t block_bases;     /* int32 [ceil(T/32), E_l] first row of block b in expert e */
   uint64_t inter;           /* e4m3  [2*R_cap, 2048] SwiGLU output, rows (2r, 2r+1) = (hi, lo) */
   uint64_t inter_scale;     /* fp32  [16, R_cap]  scale of hi; lo uses scale/16    */
   uint64_t down;            /* fp32  [R_cap, 7168] GEMM2 output per permuted row  */
+  uint64_t act;             /* e4m3  [R_cap, 7168] permuted hidden rows (GEMM1 input) */
+  uint64_t act_scale;       /* fp32  [56, R_cap]  their 1x128 scales              */
   int32_t row_capacity;     /* R_cap = T * min(8, E_l)                            */
   int32_t reserved;
 } moe_fp8_ds_layout;

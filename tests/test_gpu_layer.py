@@ -147,6 +147,10 @@ def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
     assert torch.equal(inv, inv_ref)
     row_tok = ws_view(ws, lay.row_token, max(R, 1), torch.int32)[:nrows].cpu().long()
     assert torch.equal(row_tok, row_tok_ref)
+    act = ws_view(ws, lay.act, R * 7168, torch.uint8).view(R, 7168)[:nrows].cpu()
+    assert torch.equal(act, inp["hidden_states"].view(torch.uint8)[row_tok])
+    act_sc = ws_view(ws, lay.act_scale, 56 * R, torch.float32).view(56, R)[:, :nrows].cpu()
+    assert torch.equal(act_sc, inp["hidden_states_scale"][:, row_tok])
     # GEMM1 + SwiGLU + two-term requantisation
     inter = ws_view(ws, lay.inter, 2 * R * 2048, torch.uint8).view(R, 2, 2048)[:nrows].cpu()
     isc = ws_view(ws, lay.inter_scale, 16 * R, torch.float32).view(16, R)[:, :nrows].cpu().t()
