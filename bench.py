@@ -262,6 +262,119 @@ def run_reference_arm(a, T, E_l):
     print(json.dumps(line), flush=True)
 
 
+EP_TOKENS = 8192          # tokens per step over all ranks
+
+
+def run_ep(a, world, rank, local_rank):
+    """Expert-parallel layer (config 3): 256 experts split over the ranks, 8192
+    tokens per step split evenly; dispatch/combine over NCCL.  value = all ranks'
+    tokens / max-over-ranks step time (strong scaling: total work fixed)."""
+    import torch.distributed as dist
+    dev = torch.device("cuda", local_rank)
+    pkg = graft.load_package()
+    L = sys.modules["fib_b200._lib"]
+    ep = sys.modules.get("fib_b200.ep") or __import__("fib_b200.ep", fromlist=["ep"])
+    E_l = 256 // world
+    T_l = EP_TOKENS // world
+    logits, bias, hs, hss = pkg.inputs.make_token_inputs(T_l, seed=1000 + rank, device=dev)
+    w13, s13, w2, s2 = pkg.inputs.make_expert_shard(rank * E_l, E_l, seed=0, device=dev)
+    layer = ep.from_library()
+    out = torch.empty(T_l, H, dtype=torch.bfloat16, device=dev)
+    fn = lambda: layer(logits, bias, hs, hss, w13, s13, w2, s2, 2.5, out)  # noqa: E731
+    for _ in range(a.warmup):
+        fn()
+    dist.barrier()
+    torch.cuda.synchronize()
+    clk = ClockSampler(local_rank).__enter__()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(a.steps):
+        fn()
+    ev1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk.__exit__(None, None, None)
+    ms = torch.tensor([ev0.elapsed_time(ev1) / a.steps], device=dev)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms)
+    # e2e: token inputs from pinned host memory, output read back, inside the timed region
+    h_in = [t.cpu().pin_memory() for t in (logits, hs.view(torch.uint8), hss)]
+    d_in = [torch.empty_like(t, device=dev) for t in h_in]
+    h_out = torch.empty(T_l, H, dtype=torch.bfloat16).pin_memory()
+
+    def e2e():
+        for d, h in zip(d_in, h_in):
+            d.copy_(h, non_blocking=True)
+        layer(d_in[0], bias, d_in[1].view(torch.float8_e4m3fn), d_in[2], w13, s13, w2, s2, 2.5, out)
+        h_out.copy_(out, non_blocking=True)
+    for _ in range(2):
+        e2e()
+    dist.barrier()
+    torch.cuda.synchronize()
+    ev0.record()
+    for _ in range(a.steps):
+        e2e()
+    ev1.record()
+    torch.cuda.synchronize()
+    e2e_ms = torch.tensor([ev0.elapsed_time(ev1) / a.steps], device=dev)
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    stats = layer.last_stats
+    if rank == 0:
+        line = {
+            "metric": "moe_layer_tokens_per_s", "value": EP_TOKENS / (ms * 1e-3), "unit": "tokens/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "fp8e4m3 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"ep_T{EP_TOKENS}_E256", "tokens_total": EP_TOKENS, "tokens_per_rank": T_l,
+                       "experts_per_rank": E_l, "parallelism": f"ep{world}",
+                       "collectives": "NCCL all-to-all (counts, dispatch rows, bf16 partials)",
+                       "l2": "inputs larger than L2 (weights %.1f GB per rank)" % (E_l * 44.05e-3),
+                       "rank0_sent_rows": stats.get("sent_rows"), "rank0_recv_rows": stats.get("recv_rows")},
+            "e2e": {"value": EP_TOKENS / (float(e2e_ms) * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in h_in) * world,
+                    "d2h_bytes_per_step": h_out.numel() * 2 * world, "ms_per_step": float(e2e_ms)},
+            "clocks": clk.summary(),
+            "gpu_launches": a.steps * (1 + L.load().moe_fp8_ds_launches_per_call()),
+        }
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def run_reference_arm_ep(a, world):
+    """Reference CPU path on a bounded sample of the expert-parallel workload:
+    8 tokens through all 256 experts (only the experts they pick are built)."""
+    from oracle import moe_ref
+    pkg = graft.load_package()
+    torch.set_num_threads(os.cpu_count() or 1)
+    Ts = 8
+    logits, bias, hs, hss = pkg.inputs.make_token_inputs(Ts, seed=1000)
+    ids, w, _ = moe_ref.route(logits, bias, 2.5)
+    used = sorted(set(ids.flatten().tolist()))
+    shards = {e: pkg.inputs.make_expert_shard(e, 1, seed=0) for e in used}
+    times = []
+    for step in range(a.warmup + a.steps):
+        t0 = time.perf_counter()
+        ids, w, _ = moe_ref.route(logits, bias, 2.5)
+        acc = torch.zeros(Ts, H)
+        for e, (w13, s13, w2, s2) in shards.items():
+            acc += moe_ref.experts_forward(ids, w, hs, hss, w13, s13, w2, s2, e)
+        acc.to(torch.bfloat16)
+        if step >= a.warmup:
+            times.append(time.perf_counter() - t0)
+    dt = statistics.mean(times)
+    v = Ts / dt
+    print(json.dumps({
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": f"ep_T{EP_TOKENS}_E256", "note": "bounded sample: 8 tokens, all 256 experts, host cores"},
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+                         "sample": f"{Ts} tokens through their {len(used)} experts per step"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "gpu_launches": 0}), flush=True)
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -272,7 +385,10 @@ def main():
 
     if a.impl == "reference":
         if rank == 0:
-            run_reference_arm(a, T, E_l)
+            if world > 1:
+                run_reference_arm_ep(a, world)
+            else:
+                run_reference_arm(a, T, E_l)
         return
 
     torch.cuda.set_device(local_rank)
@@ -280,6 +396,7 @@ def main():
     if world > 1:
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
+        return run_ep(a, world, rank, local_rank)
     pkg = graft.load_package()
     K = sys.modules["fib_b200.kernel"]
     L = sys.modules["fib_b200._lib"]

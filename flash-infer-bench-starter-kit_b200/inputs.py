@@ -118,6 +118,41 @@ def input_digest(inp: dict) -> str:
     return h.hexdigest()
 
 
+@torch.no_grad()
+def make_token_inputs(T: int, seed: int = 0, device: str | torch.device = "cpu", skew: float = 0.0,
+                      hot_experts=HOT_EXPERTS_DEFAULT):
+    """Token-side tensors only: (routing_logits, routing_bias, hidden_states, hidden_states_scale)."""
+    dev = torch.device(device)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    logits = torch.randn(T, E_GLOBAL, generator=g, device=dev, dtype=torch.float32)
+    if skew:
+        logits[:, list(hot_experts)] += skew
+    bias = (torch.randn(E_GLOBAL, generator=g, device=dev) * 0.1).to(torch.bfloat16)
+    hidden = torch.randn(T, H, generator=g, device=dev)
+    hs, hs_scale = quant_rows_1x128(hidden)
+    return logits, bias, hs, hs_scale
+
+
+@torch.no_grad()
+def make_expert_shard(first: int, count: int, seed: int = 0, device: str | torch.device = "cpu"):
+    """Weights of global experts [first, first+count), each drawn from its own
+    generator (seed, expert id), so any shard of the 256 experts is a slice of
+    the same full set.  Returns (w13, s13, w2, s2)."""
+    dev = torch.device(device)
+    w1 = torch.empty(count, 2 * I, H, dtype=torch.float8_e4m3fn, device=dev)
+    s1 = torch.empty(count, 2 * I // BLOCK, H // BLOCK, dtype=torch.float32, device=dev)
+    w2 = torch.empty(count, H, I, dtype=torch.float8_e4m3fn, device=dev)
+    s2 = torch.empty(count, H // BLOCK, I // BLOCK, dtype=torch.float32, device=dev)
+    for i in range(count):
+        g = torch.Generator(device=dev).manual_seed(seed * 1_000_003 + first + i)
+        w = torch.randn(2 * I, H, generator=g, device=dev) * (H ** -0.5)
+        w1[i], s1[i] = quant_block_128x128(w)
+        w = torch.randn(H, I, generator=g, device=dev) * (I ** -0.5)
+        w2[i], s2[i] = quant_block_128x128(w)
+        del w
+    return w1, s1, w2, s2
+
+
 ARG_ORDER = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale",
              "gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale",
              "local_expert_offset", "routed_scaling_factor")

@@ -130,33 +130,45 @@ def swiglu(g1: torch.Tensor) -> torch.Tensor:
 # Whole layer (moe.cu:137-240)
 # --------------------------------------------------------------------------
 @torch.no_grad()
-def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale,
-                gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
-                local_expert_offset: int, routed_scaling_factor: float,
-                return_fp32: bool = False):
-    """Reference forward on CPU.  Returns bf16 [T, H] (or the fp32 accumulator).
-
-    Only the experts that receive at least one token are dequantised, which
-    changes the cost, not the result, of the reference's full dequantisation.
-    """
-    T = routing_logits.shape[0]
+def experts_forward(topk_idx, topk_w, hidden_states, hidden_states_scale,
+                    gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                    local_expert_offset: int):
+    """Contribution of the local experts for a given routing (moe.cu:208-236):
+    fp32 [T, H] = sum over local picks, in ascending expert order, of w * expert(x)."""
+    T = hidden_states.shape[0]
     E_l = gemm1_weights.shape[0]
-    topk_idx, _, dense_w = route(routing_logits, routing_bias, routed_scaling_factor)
     A = dequant_hidden(hidden_states, hidden_states_scale)
     acc = torch.zeros(T, H, dtype=torch.float32)
     for le in range(E_l):
         ge = local_expert_offset + le
         if ge < 0 or ge >= E_GLOBAL:
             continue
-        sel = (topk_idx == ge).any(dim=1)
+        hit = topk_idx == ge
+        sel = hit.any(dim=1)
         if not bool(sel.any()):
             continue
         tok = sel.nonzero().squeeze(1)
+        w_tok = (topk_w * hit.float()).sum(dim=1).index_select(0, tok)
         W13 = dequant_weight(gemm1_weights[le], gemm1_weights_scale[le])
         W2 = dequant_weight(gemm2_weights[le], gemm2_weights_scale[le])
         g1 = A.index_select(0, tok).matmul(W13.t())
         o = swiglu(g1).matmul(W2.t())
-        acc.index_add_(0, tok, o * dense_w.index_select(0, tok)[:, ge].unsqueeze(1))
+        acc.index_add_(0, tok, o * w_tok.unsqueeze(1))
+    return acc
+
+
+@torch.no_grad()
+def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                local_expert_offset: int, routed_scaling_factor: float,
+                return_fp32: bool = False):
+    """Reference forward on CPU (moe.cu:137-240).  Returns bf16 [T, H] (or the
+    fp32 accumulator).  Only experts that receive a token are dequantised,
+    which changes the cost, not the result, of the reference's full
+    dequantisation."""
+    topk_idx, topk_w, _ = route(routing_logits, routing_bias, routed_scaling_factor)
+    acc = experts_forward(topk_idx, topk_w, hidden_states, hidden_states_scale, gemm1_weights,
+                          gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset)
     return acc if return_fp32 else acc.to(torch.bfloat16)
 
 

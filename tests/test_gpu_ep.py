@@ -1,0 +1,75 @@
+"""GPU, 2 processes over NCCL: the expert-parallel layer equals the
+single-GPU layer that holds all 256 experts (within the layer tolerance; the
+EP path adds one bf16 rounding of each rank's partial sum).  Skipped on a box
+with fewer than two GPUs."""
+
+from __future__ import annotations
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-2, 2e-2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, T, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        import __graft_entry__ as ge
+        pkg = ge.load_package()
+        ep = __import__("fib_b200.ep", fromlist=["ep"])
+        E_l = 256 // world
+        logits, bias, hs, hss = pkg.inputs.make_token_inputs(T, seed=200 + rank, device=dev)
+        w13, s13, w2, s2 = pkg.inputs.make_expert_shard(0, 256, seed=5, device=dev)
+        ref = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
+        pkg.kernel(logits, bias, hs, hss, w13, s13, w2, s2, 0, 2.5, ref)
+        sl = slice(rank * E_l, (rank + 1) * E_l)
+        layer = ep.from_library()
+        out = torch.full((T, 7168), float("nan"), dtype=torch.bfloat16, device=dev)
+        layer(logits, bias, hs, hss, w13[sl], s13[sl], w2[sl], s2[sl], 2.5, out)
+        out2 = torch.empty_like(out)
+        layer(logits, bias, hs, hss, w13[sl], s13[sl], w2[sl], s2[sl], 2.5, out2)
+        torch.cuda.synchronize()
+        r, o = ref.float(), out.float()
+        bad = int(((o - r).abs() > ATOL + RTOL * r.abs()).sum())
+        q.put((rank, bad, bool(torch.isnan(o).any()), float((o - r).abs().max()),
+               torch.equal(out.view(torch.int16), out2.view(torch.int16)), layer.last_stats))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_expert_parallel_two_gpus(cuda_dev):
+    world = 2
+    if torch.cuda.device_count() < world:
+        pytest.skip("needs two GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 48, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, bad, nan, mx, det, stats in res:
+        print(f"rank {rank}: max_abs {mx:.3e} stats {stats}")
+        assert not nan and bad == 0, f"rank {rank}: {bad} elements outside tolerance (max {mx})"
+        assert det
