@@ -142,8 +142,9 @@ class ExpertParallelMoE:
 def from_library(group=None, partial_dtype=torch.bfloat16):
     """ExpertParallelMoE whose routing and expert compute run in libmoe_fp8_ds.so."""
     import ctypes
+    import importlib
     from . import _lib
-    from . import kernel as K
+    K = importlib.import_module(__package__ + ".kernel")   # the module, not the kernel() function
 
     def route_fn(logits, bias, scale):
         T = logits.shape[0]

@@ -11,7 +11,9 @@ computation.  The CUDA expert compute is covered by the GPU tests.
 from __future__ import annotations
 
 import os
+import datetime
 import socket
+import traceback
 
 import pytest
 import torch
@@ -44,7 +46,8 @@ def _free_port():
 
 def _worker(rank, world, port, T, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
     try:
         import __graft_entry__ as ge
         pkg = ge.load_package()
@@ -71,6 +74,9 @@ def _worker(rank, world, port, T, q):
         ref = standin_experts(ids, w, hs, hss, None, None, None, None, 0, 256)
         q.put((rank, torch.equal(out.view(torch.int16), out2.view(torch.int16)),
                float((out.float() - ref).abs().max()), float(ref.abs().max()), layer.last_stats))
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -84,6 +90,8 @@ def test_ep_protocol_matches_single_process(world):
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
+    errs = [r for r in res if r[1] == "error"]
+    assert not errs, errs[0][2]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

@@ -6,7 +6,9 @@ with fewer than two GPUs."""
 from __future__ import annotations
 
 import os
+import datetime
 import socket
+import traceback
 
 import pytest
 import torch
@@ -30,7 +32,8 @@ def _worker(rank, world, port, T, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                            timeout=datetime.timedelta(seconds=60))
     try:
         import __graft_entry__ as ge
         pkg = ge.load_package()
@@ -51,6 +54,9 @@ def _worker(rank, world, port, T, q):
         bad = int(((o - r).abs() > ATOL + RTOL * r.abs()).sum())
         q.put((rank, bad, bool(torch.isnan(o).any()), float((o - r).abs().max()),
                torch.equal(out.view(torch.int16), out2.view(torch.int16)), layer.last_stats))
+    except Exception:
+        q.put((rank, "error", traceback.format_exc()))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -65,7 +71,9 @@ def test_expert_parallel_two_gpus(cuda_dev):
     procs = [ctx.Process(target=_worker, args=(r, world, port, 48, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=600) for _ in range(world)]
+    res = [q.get(timeout=300) for _ in range(world)]
+    errs = [r for r in res if r[1] == "error"]
+    assert not errs, errs[0][2]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
