@@ -93,7 +93,7 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_read_device_error.argtypes = [P, P, ctypes.POINTER(I32)]
         lib.moe_fp8_ds_status_string.argtypes = [ctypes.c_int]
         lib.moe_fp8_ds_status_string.restype = ctypes.c_char_p
-        lib.moe_fp8_ds_launches_per_call.argtypes = []
+        lib.moe_fp8_ds_launches_per_call.argtypes = [I32]
         lib.moe_fp8_ds_set_tile_override.argtypes = [I32, I32]
         lib.moe_fp8_ds_set_stage_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), I32]
         for name in EXPORTS:

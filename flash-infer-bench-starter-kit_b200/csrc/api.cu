@@ -84,8 +84,12 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->E_l = E_l;
   P->NB = (T + kPermBlock - 1) / kPermBlock;
   P->R_cap = T * (E_l < kTopK ? E_l : kTopK);
-  P->bn1 = g_bn_override[0] ? g_bn_override[0] : pick_bn(T, E_l);
-  P->bn2 = g_bn_override[1] ? g_bn_override[1] : pick_bn(T, E_l);
+  // GEMM1 keeps X1 and X2 accumulators of 128 features per token column in
+  // registers, so its widest tile is 64 tokens (128 would need the whole
+  // register file); GEMM2 holds one accumulator and goes to 128.
+  const int bn_auto = pick_bn(T, E_l);
+  P->bn1 = g_bn_override[0] ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
+  P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_auto;
   P->grid = sm_count;
   auto max_mt = [&](int bn) {
     long v = (long)P->R_cap / bn + E_l;
@@ -100,7 +104,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.topk_ids = take((uint64_t)T * kTopK * 4);
   P->pub.topk_weights = take((uint64_t)T * kTopK * 4);
   P->pub.inv_row = take((uint64_t)T * kTopK * 4);
-  P->NB8 = (T + kRouteTokens - 1) / kRouteTokens;
+  P->NB8 = 4 * P->NB;                     // byte-mask row length, padded to whole 32-token blocks
   P->pub.block_masks = take((uint64_t)P->NB8 * E_l);
   P->pub.block_bases = take((uint64_t)P->NB * E_l * 4);
   P->pub.seg_offsets = take((uint64_t)(E_l + 1) * 4);
@@ -203,18 +207,30 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     return MOE_ERR_INVALID_ARGUMENT;
 
   cudaError_t ce;
-  mark_stage(0, s);
-  ce = launch_route(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
-                    a->local_expert_offset, E_l, ids, wts, masks8, err, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
-  mark_stage(1, s);
-  ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
-                   kInter / 128, cnt2, kHidden / 128, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
-  mark_stage(2, s);
-  ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
-                      a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  if (!routed && T <= kFrontMaxTokens) {
+    // Small batch: routing, row assignment and gather in one launch.
+    mark_stage(0, s);
+    ce = launch_front(a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
+                      a->local_expert_offset, E_l, P.R_cap, P.bn1, P.bn2, kInter / 128, kHidden / 128,
+                      a->hidden_states, a->hidden_states_scale, ids, wts, masks8, P.NB8, seg, tiles1, tiles2,
+                      sched, cnt1, cnt2, inv, row_token, act, act_scale, err, s);
+    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    mark_stage(1, s);
+    mark_stage(2, s);
+  } else {
+    mark_stage(0, s);
+    ce = launch_route(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
+                      a->local_expert_offset, E_l, ids, wts, masks8, P.NB8, err, s);
+    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    mark_stage(1, s);
+    ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
+                     kInter / 128, cnt2, kHidden / 128, s);
+    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    mark_stage(2, s);
+    ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
+                        a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale, s);
+    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  }
 
   GemmParams g1{};
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
@@ -299,7 +315,7 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int3
   if (st != MOE_OK) return st;
   // No local experts (E_l = 0, no histogram): routing only.
   cudaError_t ce = launch_route(false, routing_logits, routing_bias, num_tokens,
-                                routed_scaling_factor, 0, 0, topk_ids, topk_weights, nullptr,
+                                routed_scaling_factor, 0, 0, topk_ids, topk_weights, nullptr, 0,
                                 nullptr, static_cast<cudaStream_t>(stream));
   return ce == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
@@ -313,7 +329,8 @@ int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t* device_
   if (cudaStreamSynchronize(s) != cudaSuccess) return MOE_ERR_CUDA;
   *device_error = v;
   if (v == kDevOk) return MOE_OK;
-  if (v == kDevTimeoutProducer || v == kDevTimeoutMma || v == kDevTimeoutEpilogue)
+  if (v == kDevTimeoutProducer || v == kDevTimeoutMma || v == kDevTimeoutEpilogue ||
+      v == kDevTimeoutBarrier)
     return MOE_ERR_DEVICE_TIMEOUT;
   return MOE_ERR_DEVICE_FAULT;
 }
@@ -354,6 +371,9 @@ int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
   return MOE_OK;
 }
 
-int moe_fp8_ds_launches_per_call(void) { return 6; }
+int moe_fp8_ds_launches_per_call(int32_t num_tokens) {
+  if (num_tokens <= 0) return 0;
+  return num_tokens <= kFrontMaxTokens ? 4 : 6;
+}
 
 }  // extern "C"

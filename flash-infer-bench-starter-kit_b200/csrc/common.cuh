@@ -32,6 +32,8 @@ constexpr float kFp8Max = 448.0f;
 constexpr int kPermBlock = 32;
 // Tokens routed per CTA (one warp each); four route CTAs make a permutation block.
 constexpr int kRouteTokens = 8;
+// Largest batch served by the single-launch front end (32 CTAs of 8 tokens).
+constexpr int kFrontMaxTokens = 256;
 
 // A bounded wait gives up after this many nanoseconds and raises the
 // device error word; every kernel here finishes in well under a second.
@@ -45,6 +47,7 @@ enum DeviceError : int {
   kDevTimeoutEpilogue = 3,
   kDevBadExpertId = 4,
   kDevCapacity = 5,
+  kDevTimeoutBarrier = 6,
 };
 
 // --------------------------------------------------------------------------

@@ -65,8 +65,7 @@ struct GemmCfg {
   static constexpr int NEPI = 128 * NWG;
   static constexpr int THREADS = 64 + NEPI;
   static constexpr int CPW = BN / NWG;                      // token columns per warpgroup
-  static constexpr int SUB = BN + NW;                       // scales of one K block
-  static constexpr int SLOT = KS * SUB;                     // scales of one iteration
+  static constexpr int SLOT = KS * NW * BN;                 // promotion coefficients per iteration
   static constexpr int RING = 3;                            // slots (prefetch distance 2)
   static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4;
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
@@ -74,7 +73,7 @@ struct GemmCfg {
   static_assert(TMEM_USED <= 512 && NBUF >= 2, "TMEM budget");
   static_assert(CPW % 16 == 0 || (KIND == 2 && CPW % 8 == 0), "column chunking");
   static_assert(MMA_N % 16 == 0 && MMA_N <= 256, "MMA N");
-  static_assert(SLOT <= NEPI, "one scale per epilogue thread");
+  static_assert(SLOT <= NEPI, "one coefficient per epilogue thread");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -216,12 +215,13 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     int seg_k0 = 0;
     int4 tile = make_int4(0, 0, 0, 0);
 
-    // Scales of iteration i live in ring slot i % RING; per K block kk the
-    // entries [kk*SUB, kk*SUB+BN) are token-column scales and the next NW the
-    // weight-block scales.  Thread et < SLOT loads its entry two iterations
-    // ahead, so the loads never sit on the critical path.
+    // Promotion coefficients of iteration i live in ring slot i % RING:
+    // coef[kk][w][j] = weight-block scale (K block kk, weight tile w) x
+    // token-column scale (K block kk, column j), 0 for columns past the tile.
+    // Thread et < SLOT computes its entry two iterations ahead, so the loads
+    // never sit on the critical path and the promotion is one FMA per element.
     const bool loader = et < C::SLOT;
-    const int my_kk = et / C::SUB, my_e = et % C::SUB;
+    const int my_kk = et / (C::NW * BN), my_w = (et / BN) % C::NW, my_j = et % BN;
     int pf_unit = -1, pf_col = -1, pf_e = 0, pf_nt = 0;
     auto fetch = [&](int i_t) -> float {
       const int it_t = sch.it0 + i_t;
@@ -232,12 +232,12 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         const int4 tl = p.tiles[u_t % sch.n_mt];
         pf_e = tl.x;
         pf_nt = u_t / sch.n_mt;
-        pf_col = (my_e < BN && my_e < tl.z) ? tl.y + my_e : -1;
+        pf_col = my_j < tl.z ? tl.y + my_j : -1;
       }
-      if (my_e < BN) return pf_col >= 0 ? __ldg(p.b_scale + (size_t)kb_t * p.R_cap + pf_col) : 0.f;
-      const int w = my_e - BN;
-      const int nb = KIND == 1 ? pf_nt + w * (kInter / 128) : pf_nt;
-      return __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
+      if (pf_col < 0) return 0.f;
+      const int nb = KIND == 1 ? pf_nt + my_w * (kInter / 128) : pf_nt;
+      const float wsc = __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
+      return wsc * __ldg(p.b_scale + (size_t)kb_t * p.R_cap + pf_col);
     };
     for (int i_t = 0; i_t < 2 && i_t < n_iter; ++i_t)
       if (loader) sring[i_t * C::SLOT + et] = fetch(i_t);
@@ -263,34 +263,53 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
-          const float* sb = sl + kk * C::SUB;
 #pragma unroll
           for (int w = 0; w < C::NW; ++w) {
-            const float wsc = sb[BN + w];
+            const float* coef = sl + (kk * C::NW + w) * BN + j0;
             const uint32_t col0 = (uint32_t)(b * C::BUF_COLS + (kk * C::NW + w) * C::MMA_N);
             if (KIND == 1) {
+              // 16 token columns per TMEM load, two loads in flight per wait
 #pragma unroll
-              for (int c = 0; c < C::CPW / 16; ++c) {
-                float v[16];
-                tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v);
+              for (int c = 0; c < C::CPW / 16; c += 2) {
+                float v[2][16];
+                tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v[0]);
+                if (c + 1 < C::CPW / 16) tmem_ld16(tmem_base + lane_addr + col0 + j0 + (c + 1) * 16, v[1]);
                 tmem_ld_wait();
 #pragma unroll
-                for (int x = 0; x < 16; ++x) {
-                  const int jj = c * 16 + x;
-                  acc[w][jj] = fmaf(v[x], wsc * sb[j0 + jj], acc[w][jj]);
+                for (int h = 0; h < 2; ++h) {
+                  if (c + h >= C::CPW / 16) break;
+#pragma unroll
+                  for (int x4 = 0; x4 < 4; ++x4) {
+                    const float4 cf = reinterpret_cast<const float4*>(coef + (c + h) * 16)[x4];
+                    const int jj = (c + h) * 16 + x4 * 4;
+                    acc[w][jj + 0] = fmaf(v[h][x4 * 4 + 0], cf.x, acc[w][jj + 0]);
+                    acc[w][jj + 1] = fmaf(v[h][x4 * 4 + 1], cf.y, acc[w][jj + 1]);
+                    acc[w][jj + 2] = fmaf(v[h][x4 * 4 + 2], cf.z, acc[w][jj + 2]);
+                    acc[w][jj + 3] = fmaf(v[h][x4 * 4 + 3], cf.w, acc[w][jj + 3]);
+                  }
                 }
               }
             } else {
+              // TMEM columns (2j, 2j+1) = (hi, lo) of token j: 8 tokens per load
 #pragma unroll
-              for (int c = 0; c < C::CPW / 8; ++c) {
-                float v[16];
-                tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v);
+              for (int c = 0; c < C::CPW / 8; c += 2) {
+                float v[2][16];
+                tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v[0]);
+                if (c + 1 < C::CPW / 8) tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + (c + 1) * 16, v[1]);
                 tmem_ld_wait();
 #pragma unroll
-                for (int x = 0; x < 8; ++x) {
-                  const int jj = c * 8 + x;
-                  const float pv = fmaf(v[2 * x + 1], 0.0625f, v[2 * x]);
-                  acc[w][jj] = fmaf(pv, wsc * sb[j0 + jj], acc[w][jj]);
+                for (int h = 0; h < 2; ++h) {
+                  if (c + h >= C::CPW / 8) break;
+#pragma unroll
+                  for (int x4 = 0; x4 < 2; ++x4) {
+                    const float4 cf = reinterpret_cast<const float4*>(coef + (c + h) * 8)[x4];
+                    const int jj = (c + h) * 8 + x4 * 4;
+                    const float* vv = v[h] + x4 * 8;
+                    acc[w][jj + 0] = fmaf(fmaf(vv[1], 0.0625f, vv[0]), cf.x, acc[w][jj + 0]);
+                    acc[w][jj + 1] = fmaf(fmaf(vv[3], 0.0625f, vv[2]), cf.y, acc[w][jj + 1]);
+                    acc[w][jj + 2] = fmaf(fmaf(vv[5], 0.0625f, vv[4]), cf.z, acc[w][jj + 2]);
+                    acc[w][jj + 3] = fmaf(fmaf(vv[7], 0.0625f, vv[6]), cf.w, acc[w][jj + 3]);
+                  }
                 }
               }
             }
@@ -403,7 +422,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 template <int KIND, int BN> struct Pick;
 template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2; };
 template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2; };
-template <> struct Pick<1, 64> { static constexpr int S = 5, W = 1, K = 1; };
+template <> struct Pick<1, 64> { static constexpr int S = 5, W = 2, K = 1; };
 template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1; };
 template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2; };
 template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2; };

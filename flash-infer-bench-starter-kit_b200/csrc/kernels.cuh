@@ -32,14 +32,22 @@ cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtenso
 
 cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
                          float scaling, int local_offset, int E_l, int32_t* ids, float* w,
-                         uint8_t* masks8, int* err, cudaStream_t st);
-cudaError_t launch_scan(const uint8_t* masks8, int NB8, int32_t* bases, int NB, int E_l, int32_t* seg,
+                         uint8_t* masks8, int NB8p, int* err, cudaStream_t st);
+cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
                         int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st);
-cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8, const int32_t* bases, int T,
+cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
                            uint8_t* act, float* act_scale, cudaStream_t st);
+// Routing + row assignment + activation gather in one launch, T <= kFrontMaxTokens.
+cudaError_t launch_front(const float* logits, const void* bias, int T, float scaling, int local_offset,
+                         int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2, const void* hidden,
+                         const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
+                         int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
+                         int32_t* counters1, int32_t* counters2, int32_t* inv_row,
+                         int32_t* row_token, uint8_t* act, float* act_scale, int* err,
+                         cudaStream_t st);
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
                            void* out, float* out_f32, cudaStream_t st);
 

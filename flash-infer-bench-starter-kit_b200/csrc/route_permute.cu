@@ -27,17 +27,152 @@ namespace moe {
 // accumulators, lanes summed last), so weights match the reference's own
 // fp32 arithmetic.  Ties in any top-k go to the lower index.
 //
-// One CTA routes kRouteTokens tokens and writes the byte masks8[g][e], bit
-// w set when token 8g+w picked local expert e.  Four consecutive bytes form
-// the 32-token permutation-block mask the scan turns into row offsets and
-// the scatter into each token's rank inside its expert (ascending tokens).
+// One CTA routes kRouteTokens tokens and writes the byte masks8[e][g], bit
+// w set when token 8g+w picked local expert e (rows of NB8p = 4*ceil(T/32)
+// bytes, zero-padded).  Four consecutive bytes form the 32-token
+// permutation-block mask that the scan turns into row offsets and the scatter
+// into each token's rank inside its expert (ascending tokens).
 // --------------------------------------------------------------------------
+// Routes token t with one warp; returns the token's k-th expert id (ascending)
+// in lane k < 8 and -1 elsewhere, and writes ids/weights unless kFromIds.
+template <bool kFromIds>
+__device__ __forceinline__ int route_token(int t, int lane, const float* __restrict__ logits,
+                                           const __nv_bfloat16* __restrict__ bias, float scaling,
+                                           int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
+                                           int* __restrict__ err) {
+  int my_id = -1;  // lane k < 8 ends up holding the k-th id (ascending)
+  if constexpr (!kFromIds) {
+    const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExpertsGlobal) + lane * 2;
+    float4 l0 = lp[0], l1 = lp[1];
+    float x[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+    uint4 braw = reinterpret_cast<const uint4*>(bias)[lane];
+    const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&braw);
+    float s[8], sb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float e = (float)exp(-(double)x[j]);
+      s[j] = __frcp_rn(__fadd_rn(1.0f, e));
+      sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
+    }
+    // ---- group score: sum of the top-2 sb of each 32-expert group
+    float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = sb[j];
+      if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
+    }
+#pragma unroll
+    for (int off = 1; off <= 2; off <<= 1) {
+      float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+      float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+      float n1, n2;
+      if (m1 >= o1) { n1 = m1; n2 = fmaxf(m2, o1); } else { n1 = o1; n2 = fmaxf(m1, o2); }
+      m1 = n1; m2 = n2;
+    }
+    const float gscore = __fadd_rn(m1, m2);
+    // ---- keep the best 4 groups (ties: lower group)
+    float gs[kGroups];
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
+    unsigned keep = 0;
+#pragma unroll
+    for (int r = 0; r < kTopKGroups; ++r) {
+      int best = -1; float bv = -INFINITY;
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+        if (!((keep >> g) & 1u) && (best < 0 || gs[g] > bv)) { best = g; bv = gs[g]; }
+      keep |= 1u << best;
+    }
+    const bool my_group_kept = (keep >> (lane >> 2)) & 1u;
+    // ---- top-8 experts of sb inside kept groups
+    float cand[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cand[j] = my_group_kept ? sb[j] : -INFINITY;
+    unsigned taken = 0;
+    int sel_e[kTopK];
+    float sel_s[kTopK];
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      int bj = -1; float bv = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) { bj = j; bv = cand[j]; }
+      int be = lane * 8 + bj;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+        int oe = __shfl_xor_sync(0xffffffffu, be, off);
+        if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+      }
+      float my_s = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) if (be == lane * 8 + j) { taken |= 1u << j; my_s = s[j]; }
+      sel_e[k] = be;
+      sel_s[k] = __shfl_sync(0xffffffffu, my_s, be >> 3);
+    }
+    // ---- sort the 8 picks ascending (all lanes hold the same arrays)
+#pragma unroll
+    for (int a = 1; a < kTopK; ++a)
+#pragma unroll
+      for (int b = a; b > 0; --b)
+        if (sel_e[b] < sel_e[b - 1]) {
+          int te = sel_e[b]; sel_e[b] = sel_e[b - 1]; sel_e[b - 1] = te;
+          float ts = sel_s[b]; sel_s[b] = sel_s[b - 1]; sel_s[b - 1] = ts;
+        }
+    // ---- normaliser in torch's CPU reduction order: lane l (< 8) forms the
+    // vector-lane partial P_l = ((A0+A1)+A2)+A3 with A_q = sum (ascending
+    // expert id) of picks e with e%8 == l and (e/8)%4 == q.
+    float P = 0.f;
+    if (lane < 8) {
+      float A[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k)
+        if ((sel_e[k] & 7) == lane) {
+          int q = (sel_e[k] >> 3) & 3;
+#pragma unroll
+          for (int qq = 0; qq < 4; ++qq) if (qq == q) A[qq] = __fadd_rn(A[qq], sel_s[k]);
+        }
+      P = __fadd_rn(__fadd_rn(__fadd_rn(A[0], A[1]), A[2]), A[3]);
+    }
+    float total = 0.f;
+#pragma unroll
+    for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, P, l));
+    const float denom = __fadd_rn(total, 1e-20f);
+    if (lane < kTopK) {
+      float my_w = 0.f; int my_e = 0;
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) if (k == lane) { my_e = sel_e[k]; my_w = sel_s[k]; }
+      my_w = __fmul_rn(__fdiv_rn(my_w, denom), scaling);
+      topk_ids[(size_t)t * kTopK + lane] = my_e;
+      topk_w[(size_t)t * kTopK + lane] = my_w;
+      my_id = my_e;
+    }
+  } else {
+    if (lane < kTopK) {
+      my_id = topk_ids[(size_t)t * kTopK + lane];
+      if (my_id < 0 || my_id >= kExpertsGlobal) { raise_error(err, kDevBadExpertId); my_id = -1; }
+    }
+  }
+  return my_id;
+}
+
+// CTA g stores its byte of every expert row; the last CTA zeroes the padding.
+__device__ __forceinline__ void store_masks(uint8_t* __restrict__ masks8, int NB8p, int E_l,
+                                            const uint32_t* s_mask) {
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
+    uint8_t* row = masks8 + (size_t)e * NB8p;
+    row[blockIdx.x] = static_cast<uint8_t>(s_mask[e]);
+    if (blockIdx.x == gridDim.x - 1)
+      for (int g = gridDim.x; g < NB8p; ++g) row[g] = 0;
+  }
+}
+
 template <bool kFromIds>
 __global__ void __launch_bounds__(kRouteTokens * 32)
 route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias,
              int T, float scaling, int local_offset, int E_l,
              int32_t* __restrict__ topk_ids, float* __restrict__ topk_w,
-             uint8_t* __restrict__ masks8, int* __restrict__ err) {
+             uint8_t* __restrict__ masks8, int NB8p, int* __restrict__ err) {
   __shared__ uint32_t s_mask[kExpertsGlobal];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -48,140 +183,21 @@ route_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
 
   const int t = blockIdx.x * kRouteTokens + warp;
   if (t < T) {
-    int my_id = -1;  // lane k < 8 ends up holding the k-th id (ascending)
-    if constexpr (!kFromIds) {
-      const float4* lp = reinterpret_cast<const float4*>(logits + (size_t)t * kExpertsGlobal) + lane * 2;
-      float4 l0 = lp[0], l1 = lp[1];
-      float x[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
-      uint4 braw = reinterpret_cast<const uint4*>(bias)[lane];
-      const __nv_bfloat16* bb = reinterpret_cast<const __nv_bfloat16*>(&braw);
-      float s[8], sb[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float e = (float)exp(-(double)x[j]);
-        s[j] = __frcp_rn(__fadd_rn(1.0f, e));
-        sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
-      }
-      // ---- group score: sum of the top-2 sb of each 32-expert group
-      float m1 = -INFINITY, m2 = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float v = sb[j];
-        if (v > m1) { m2 = m1; m1 = v; } else if (v > m2) { m2 = v; }
-      }
-#pragma unroll
-      for (int off = 1; off <= 2; off <<= 1) {
-        float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
-        float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
-        float n1, n2;
-        if (m1 >= o1) { n1 = m1; n2 = fmaxf(m2, o1); } else { n1 = o1; n2 = fmaxf(m1, o2); }
-        m1 = n1; m2 = n2;
-      }
-      const float gscore = __fadd_rn(m1, m2);
-      // ---- keep the best 4 groups (ties: lower group)
-      float gs[kGroups];
-#pragma unroll
-      for (int g = 0; g < kGroups; ++g) gs[g] = __shfl_sync(0xffffffffu, gscore, 4 * g);
-      unsigned keep = 0;
-#pragma unroll
-      for (int r = 0; r < kTopKGroups; ++r) {
-        int best = -1; float bv = -INFINITY;
-#pragma unroll
-        for (int g = 0; g < kGroups; ++g)
-          if (!((keep >> g) & 1u) && (best < 0 || gs[g] > bv)) { best = g; bv = gs[g]; }
-        keep |= 1u << best;
-      }
-      const bool my_group_kept = (keep >> (lane >> 2)) & 1u;
-      // ---- top-8 experts of sb inside kept groups
-      float cand[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cand[j] = my_group_kept ? sb[j] : -INFINITY;
-      unsigned taken = 0;
-      int sel_e[kTopK];
-      float sel_s[kTopK];
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        int bj = -1; float bv = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) { bj = j; bv = cand[j]; }
-        int be = lane * 8 + bj;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-          float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-          int oe = __shfl_xor_sync(0xffffffffu, be, off);
-          if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
-        }
-        float my_s = 0.f;
-#pragma unroll
-        for (int j = 0; j < 8; ++j) if (be == lane * 8 + j) { taken |= 1u << j; my_s = s[j]; }
-        sel_e[k] = be;
-        sel_s[k] = __shfl_sync(0xffffffffu, my_s, be >> 3);
-      }
-      // ---- sort the 8 picks ascending (all lanes hold the same arrays)
-#pragma unroll
-      for (int a = 1; a < kTopK; ++a)
-#pragma unroll
-        for (int b = a; b > 0; --b)
-          if (sel_e[b] < sel_e[b - 1]) {
-            int te = sel_e[b]; sel_e[b] = sel_e[b - 1]; sel_e[b - 1] = te;
-            float ts = sel_s[b]; sel_s[b] = sel_s[b - 1]; sel_s[b - 1] = ts;
-          }
-      // ---- normaliser in torch's CPU reduction order: lane l (< 8) forms the
-      // vector-lane partial P_l = ((A0+A1)+A2)+A3 with A_q = sum (ascending
-      // expert id) of picks e with e%8 == l and (e/8)%4 == q.
-      float P = 0.f;
-      if (lane < 8) {
-        float A[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k)
-          if ((sel_e[k] & 7) == lane) {
-            int q = (sel_e[k] >> 3) & 3;
-#pragma unroll
-            for (int qq = 0; qq < 4; ++qq) if (qq == q) A[qq] = __fadd_rn(A[qq], sel_s[k]);
-          }
-        P = __fadd_rn(__fadd_rn(__fadd_rn(A[0], A[1]), A[2]), A[3]);
-      }
-      float total = 0.f;
-#pragma unroll
-      for (int l = 0; l < 8; ++l) total = __fadd_rn(total, __shfl_sync(0xffffffffu, P, l));
-      const float denom = __fadd_rn(total, 1e-20f);
-      if (lane < kTopK) {
-        float my_w = 0.f; int my_e = 0;
-#pragma unroll
-        for (int k = 0; k < kTopK; ++k) if (k == lane) { my_e = sel_e[k]; my_w = sel_s[k]; }
-        my_w = __fmul_rn(__fdiv_rn(my_w, denom), scaling);
-        topk_ids[(size_t)t * kTopK + lane] = my_e;
-        topk_w[(size_t)t * kTopK + lane] = my_w;
-        my_id = my_e;
-      }
-    } else {
-      if (lane < kTopK) {
-        my_id = topk_ids[(size_t)t * kTopK + lane];
-        if (my_id < 0 || my_id >= kExpertsGlobal) { raise_error(err, kDevBadExpertId); my_id = -1; }
-      }
-    }
+    const int my_id = route_token<kFromIds>(t, lane, logits, bias, scaling, topk_ids, topk_w, err);
     if (lane < kTopK && my_id >= 0) {
       int le = my_id - local_offset;
       if (le >= 0 && le < E_l) atomicOr(&s_mask[le], 1u << warp);
     }
   }
   __syncthreads();
-  if (masks8)
-    for (int e = threadIdx.x; e < E_l; e += blockDim.x)
-      masks8[(size_t)blockIdx.x * E_l + e] = static_cast<uint8_t>(s_mask[e]);
+  if (masks8) store_masks(masks8, NB8p, E_l, s_mask);
 }
 
 // 32-token block mask of block b for expert e from the four byte masks.
-__device__ __forceinline__ uint32_t block_mask(const uint8_t* __restrict__ masks8, int NB8, int E_l,
+__device__ __forceinline__ uint32_t block_mask(const uint8_t* __restrict__ masks8, int NB8p, int E_l,
                                                int b, int e) {
-  uint32_t m = 0;
-#pragma unroll
-  for (int q = 0; q < kPermBlock / kRouteTokens; ++q) {
-    const int g = b * (kPermBlock / kRouteTokens) + q;
-    if (g < NB8) m |= (uint32_t)masks8[(size_t)g * E_l + e] << (q * kRouteTokens);
-  }
-  return m;
+  (void)E_l;
+  return __ldcg(reinterpret_cast<const unsigned int*>(masks8 + (size_t)e * NB8p) + b);
 }
 
 // --------------------------------------------------------------------------
@@ -222,7 +238,7 @@ __device__ void warp0_scan_inplace(int* v, int n, int* total_out) {
 }
 
 __global__ void __launch_bounds__(1024)
-scan_kernel(const uint8_t* __restrict__ masks8, int NB8, int32_t* __restrict__ bases, int NB, int E_l,
+scan_kernel(const uint8_t* __restrict__ masks8, int NB8p, int32_t* __restrict__ bases, int NB, int E_l,
             int32_t* __restrict__ seg_out,
             int bn1, int bn2, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
             int32_t* __restrict__ sched, int32_t* __restrict__ counters1, int nt1,
@@ -243,7 +259,7 @@ scan_kernel(const uint8_t* __restrict__ masks8, int NB8, int32_t* __restrict__ b
     int run = 0;
     for (int b0 = 0; b0 < NB; b0 += 32) {
       int b = b0 + lane;
-      int v = b < NB ? __popc(block_mask(masks8, NB8, E_l, b, e)) : 0;
+      int v = b < NB ? __popc(block_mask(masks8, NB8p, E_l, b, e)) : 0;
       int tot;
       int ex = warp_exclusive_scan(v, lane, &tot);
       if (b < NB) bases[(size_t)b * E_l + e] = run + ex;   // relative to segment start
@@ -305,7 +321,7 @@ constexpr int kGatherChunk = 256;                          // bytes per CTA colu
 constexpr int kGatherChunks = kHidden / kGatherChunk;      // 28
 
 __global__ void __launch_bounds__(kPermBlock * kTopK)
-scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__ masks8, int NB8,
+scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__ masks8, int NB8p,
                const int32_t* __restrict__ bases, int T, int E_l, int local_offset, int R_cap,
                const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
                int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
@@ -321,7 +337,7 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
     if (le >= 0 && le < E_l) {
       const int w = t - blockIdx.x * kPermBlock;
       const size_t be = (size_t)blockIdx.x * E_l + le;
-      row = bases[be] + __popc(block_mask(masks8, NB8, E_l, blockIdx.x, le) & ((1u << w) - 1u));
+      row = bases[be] + __popc(block_mask(masks8, NB8p, E_l, blockIdx.x, le) & ((1u << w) - 1u));
     }
     if (blockIdx.y == 0) {
       inv_row[i] = row;
@@ -349,6 +365,175 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
 #pragma unroll
     for (int q = 0; q < kGatherChunk / kBlock; ++q)
       act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + tok);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Fused front end for small batches (T <= kFrontMaxTokens): routing, row
+// assignment and activation gather in ONE launch instead of three.
+//
+// CTA g routes tokens 8g..8g+7 (one warp each) and publishes its byte masks;
+// after a grid-wide barrier every CTA recomputes the per-expert row offsets
+// from all masks (at most 32 x E_l bytes, cheaper than another launch), then
+// assigns rows to its own tokens and copies their hidden rows and scales into
+// the permuted activation.  CTA 0 also writes the segment offsets, the GEMM
+// tile lists and zeroes the stream-K counters.  All CTAs are resident (at
+// most 32 small CTAs); the barrier wait is bounded and raises the device error
+// word instead of hanging.
+// --------------------------------------------------------------------------
+__device__ bool grid_barrier(int* count, volatile int* gen, int* err) {
+  __shared__ int s_ok;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const int g = *gen;
+    __threadfence();
+    if (atomicAdd(count, 1) == (int)gridDim.x - 1) {
+      atomicExch(count, 0);
+      __threadfence();
+      atomicAdd(const_cast<int*>(gen), 1);
+    } else {
+      const unsigned long long t0 = globaltimer_ns();
+      while (*gen == g) {
+        if (globaltimer_ns() - t0 > kWaitLimitNs) { ok = 0; raise_error(err, kDevTimeoutBarrier); break; }
+        __nanosleep(64);
+      }
+    }
+    __threadfence();
+    s_ok = ok;
+  }
+  __syncthreads();
+  return s_ok != 0;
+}
+
+__global__ void __launch_bounds__(kRouteTokens * 32)
+front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ bias, int T,
+             float scaling, int local_offset, int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2,
+             const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
+             int32_t* __restrict__ topk_ids, float* __restrict__ topk_w, uint8_t* __restrict__ masks8,
+             int NB8p, int32_t* __restrict__ seg_out, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
+             int32_t* __restrict__ sched, int32_t* __restrict__ counters1,
+             int32_t* __restrict__ counters2, int32_t* __restrict__ inv_row,
+             int32_t* __restrict__ row_token, uint8_t* __restrict__ act, float* __restrict__ act_scale,
+             int* __restrict__ err) {
+  __shared__ uint32_t s_mask[kExpertsGlobal];
+  __shared__ int s_seg[kExpertsGlobal + 1];
+  __shared__ int s_base[kExpertsGlobal];
+  __shared__ int s_t1[kExpertsGlobal], s_t2[kExpertsGlobal];
+  __shared__ int2 s_list[kRouteTokens * kTopK];
+  __shared__ int s_tot[3];
+  __shared__ int s_n;
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  griddep_wait();
+  griddep_launch_dependents();
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
+  if (threadIdx.x == 0) s_n = 0;
+  __syncthreads();
+  // ---- phase 1: route own tokens, publish masks
+  const int t = blockIdx.x * kRouteTokens + warp;
+  int my_id = -1;
+  if (t < T) {
+    my_id = route_token<false>(t, lane, logits, bias, scaling, topk_ids, topk_w, err);
+    if (lane < kTopK && my_id >= 0) {
+      const int le = my_id - local_offset;
+      if (le >= 0 && le < E_l) atomicOr(&s_mask[le], 1u << warp);
+    }
+  }
+  __syncthreads();
+  store_masks(masks8, NB8p, E_l, s_mask);
+  if (!grid_barrier(err + 1, err + 2, err)) return;
+  // ---- phase 2: per-expert counts and this CTA's first row per expert
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
+    const unsigned int* row = reinterpret_cast<const unsigned int*>(masks8 + (size_t)e * NB8p);
+    const int g0 = blockIdx.x;
+    int before = 0, total = 0;
+#pragma unroll
+    for (int q = 0; q < kFrontMaxTokens / kPermBlock; ++q) {
+      if (q * 4 >= NB8p) break;
+      const uint32_t m = __ldcg(row + q);
+      total += __popc(m);
+      if (4 * q + 4 <= g0) before += __popc(m);
+      else if (4 * q < g0) before += __popc(m & ((1u << (8 * (g0 - 4 * q))) - 1u));
+    }
+    s_seg[e] = total;
+    s_base[e] = before;
+    s_t1[e] = (total + bn1 - 1) / bn1;
+    s_t2[e] = (total + bn2 - 1) / bn2;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int tot;
+    warp0_scan_inplace(s_seg, E_l, &tot);
+    if (lane == 0) { s_seg[E_l] = tot; s_tot[0] = tot; }
+  } else if (warp == 1 && blockIdx.x == 0) {
+    int tot;
+    warp0_scan_inplace(s_t1, E_l, &tot);
+    if (lane == 0) s_tot[1] = tot;
+  } else if (warp == 2 && blockIdx.x == 0) {
+    int tot;
+    warp0_scan_inplace(s_t2, E_l, &tot);
+    if (lane == 0) s_tot[2] = tot;
+  }
+  __syncthreads();
+  if (blockIdx.x == 0) {
+    for (int e = threadIdx.x; e <= E_l; e += blockDim.x) seg_out[e] = s_seg[e];
+    for (int e = warp; e < E_l; e += blockDim.x / 32) {
+      const int cnt = s_seg[e + 1] - s_seg[e], r0 = s_seg[e];
+      const int n1 = (cnt + bn1 - 1) / bn1, n2 = (cnt + bn2 - 1) / bn2;
+      for (int m = lane; m < n1; m += 32)
+        tiles1[s_t1[e] + m] = make_int4(e, r0 + m * bn1, min(bn1, cnt - m * bn1), 0);
+      for (int m = lane; m < n2; m += 32)
+        tiles2[s_t2[e] + m] = make_int4(e, r0 + m * bn2, min(bn2, cnt - m * bn2), 0);
+    }
+    const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
+    for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
+    for (int i = threadIdx.x; i < units2; i += blockDim.x) counters2[i] = 0;
+    if (threadIdx.x == 0) { sched[0] = s_tot[1]; sched[1] = s_tot[2]; sched[2] = s_tot[0]; }
+  }
+  // ---- phase 3: rows of own tokens, inverse map, activation gather
+  if (threadIdx.x < kRouteTokens * kTopK) {
+    const int w8 = threadIdx.x / kTopK, k = threadIdx.x % kTopK;
+    const int tt = blockIdx.x * kRouteTokens + w8;
+    if (tt < T) {
+      int row = -1;
+      const int le = topk_ids[(size_t)tt * kTopK + k] - local_offset;
+      if (le >= 0 && le < E_l) {
+        row = s_seg[le] + s_base[le] + __popc(s_mask[le] & ((1u << w8) - 1u));
+        row_token[row] = tt;
+        s_list[atomicAdd(&s_n, 1)] = make_int2(row, tt);
+      }
+      inv_row[(size_t)tt * kTopK + k] = row;
+    }
+  }
+  __syncthreads();
+  // copy with all of a thread's loads in flight before its stores
+  constexpr int kVec = kHidden / 16;
+  constexpr int kBatch = 8;
+  const int nvec = s_n * kVec;
+  for (int v0 = 0; v0 < nvec; v0 += kBatch * blockDim.x) {
+    uint4 buf[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int v = v0 + u * blockDim.x + threadIdx.x;
+      if (v < nvec) {
+        const int2 rt = s_list[v / kVec];
+        buf[u] = __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)rt.y * kHidden) + v % kVec);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int v = v0 + u * blockDim.x + threadIdx.x;
+      if (v < nvec) {
+        const int2 rt = s_list[v / kVec];
+        reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden)[v % kVec] = buf[u];
+      }
+    }
+  }
+  for (int v = threadIdx.x; v < s_n * kHiddenBlocks; v += blockDim.x) {
+    const int2 rt = s_list[v / kHiddenBlocks];
+    const int kb = v % kHiddenBlocks;
+    act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
   }
 }
 
@@ -402,33 +587,48 @@ combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_r
 // --------------------------------------------------------------------------
 cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
                          float scaling, int local_offset, int E_l, int32_t* ids, float* w,
-                         uint8_t* masks8, int* err, cudaStream_t st) {
+                         uint8_t* masks8, int NB8p, int* err, cudaStream_t st) {
   const int nb = (T + kRouteTokens - 1) / kRouteTokens;
   if (nb == 0) return cudaSuccess;
   const __nv_bfloat16* b = static_cast<const __nv_bfloat16*>(bias);
   if (from_ids)
     return launch_pdl(route_kernel<true>, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits, b, T,
-                      scaling, local_offset, E_l, ids, w, masks8, err);
+                      scaling, local_offset, E_l, ids, w, masks8, NB8p, err);
   return launch_pdl(route_kernel<false>, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits, b, T,
-                    scaling, local_offset, E_l, ids, w, masks8, err);
+                    scaling, local_offset, E_l, ids, w, masks8, NB8p, err);
 }
 
-cudaError_t launch_scan(const uint8_t* masks8, int NB8, int32_t* bases, int NB, int E_l, int32_t* seg,
+cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
                         int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st) {
-  return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks8, NB8, bases, NB, E_l, seg, bn1, bn2,
+  return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks8, NB8p, bases, NB, E_l, seg, bn1, bn2,
                     tiles1, tiles2, sched, counters1, nt1, counters2, nt2);
 }
 
-cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8, const int32_t* bases, int T,
+cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
                            uint8_t* act, float* act_scale, cudaStream_t st) {
   const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
   return launch_pdl(scatter_kernel, dim3(nb, kGatherChunks), dim3(kPermBlock * kTopK), 0, st, ids,
-                    masks8, NB8, bases, T, E_l, local_offset, R_cap, static_cast<const uint8_t*>(hidden),
+                    masks8, NB8p, bases, T, E_l, local_offset, R_cap, static_cast<const uint8_t*>(hidden),
                     hs_scale, inv_row, row_token, act, act_scale);
+}
+
+cudaError_t launch_front(const float* logits, const void* bias, int T, float scaling, int local_offset,
+                         int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2, const void* hidden,
+                         const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
+                         int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
+                         int32_t* counters1, int32_t* counters2, int32_t* inv_row,
+                         int32_t* row_token, uint8_t* act, float* act_scale, int* err,
+                         cudaStream_t st) {
+  const int nb = (T + kRouteTokens - 1) / kRouteTokens;
+  if (nb == 0) return cudaSuccess;
+  return launch_pdl(front_kernel, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits,
+                    static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, R_cap, bn1,
+                    bn2, nt1, nt2, static_cast<const uint8_t*>(hidden), hs_scale, ids, w, masks8, NB8p, seg,
+                    tiles1, tiles2, sched, counters1, counters2, inv_row, row_token, act, act_scale, err);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,

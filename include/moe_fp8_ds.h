@@ -90,7 +90,7 @@ typedef struct moe_fp8_ds_layout {
   uint64_t inv_row;         /* int32 [T, 8]   permuted row of (t,k) or -1         */
   uint64_t seg_offsets;     /* int32 [E_l+1]  rows of local expert e              */
   uint64_t row_token;       /* int32 [R_cap]  source token of each permuted row   */
-  uint64_t block_masks;     /* uint8 [ceil(T/8), E_l]  bit w: token 8g+w picked e  */
+  uint64_t block_masks;     /* uint8 [E_l, 4*ceil(T/32)] bit w: token 8g+w picked e */
   uint64_t block_bases;     /* int32 [ceil(T/32), E_l] first row of block b in expert e */
   uint64_t inter;           /* e4m3  [2*R_cap, 2048] SwiGLU output, rows (2r, 2r+1) = (hi, lo) */
   uint64_t inter_scale;     /* fp32  [16, R_cap]  scale of hi; lo uses scale/16    */
@@ -155,13 +155,18 @@ MOE_API const char* moe_fp8_ds_status_string(int status);
 MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Profiling hook: when `count` is 7, later calls on this process record
- * events[0..6] (cudaEvent_t handles) on the call's stream before each of
- * the six launches and after the last, so a caller can time every kernel;
+ * events[0..6] (cudaEvent_t handles) on the call's stream around the stages
+ * route | scan | scatter | GEMM1 | GEMM2 | combine (for T <= 256 the first
+ * three share one launch, timed by events 0..1; events 1 and 2 are then
+ * recorded back to back),
+ * so a caller can time every kernel;
  * count 0 turns it off.  The events must outlive the calls that use them. */
 MOE_API int moe_fp8_ds_set_stage_events(void* const* events, int32_t count);
 
-/* Number of kernel launches one moe_fp8_ds_run call enqueues. */
-MOE_API int moe_fp8_ds_launches_per_call(void);
+/* Number of kernel launches one moe_fp8_ds_run call with T tokens enqueues
+ * (4 for T <= 256, where routing, row assignment and the activation gather
+ * share one launch; 6 above; moe_fp8_ds_run_routed always enqueues 6). */
+MOE_API int moe_fp8_ds_launches_per_call(int32_t num_tokens);
 
 #ifdef __cplusplus
 }

@@ -124,6 +124,7 @@ STAGE_CASES = [
     (200, 8, 0, 14, 3.0, (32, 64)),
     (200, 8, 0, 14, 3.0, (128, 128)),
     (130, 16, 16, 15, 0.0, (64, 32)),
+    (300, 8, 0, 16, 0.0, (0, 0)),          # above the single-launch front end: 3-kernel path
 ]
 
 

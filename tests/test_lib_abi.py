@@ -48,7 +48,8 @@ def test_status_strings(pkg):
     assert lib.moe_fp8_ds_status_string(0) == b"ok"
     for st in range(1, 9):
         assert lib.moe_fp8_ds_status_string(st) != b"unknown status"
-    assert lib.moe_fp8_ds_launches_per_call() == 6
+    assert lib.moe_fp8_ds_launches_per_call(64) == 4
+    assert lib.moe_fp8_ds_launches_per_call(4096) == 6
 
 
 def test_argument_validation_without_gpu(pkg):
