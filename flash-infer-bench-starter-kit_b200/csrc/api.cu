@@ -72,8 +72,8 @@ int pick_bn(int T, int E_l) {
 
 struct Plan {
   moe_fp8_ds_layout pub;
-  int T, E_l, NB, NB8, R_cap, bn1, bn2, grid, max_mt1, max_mt2;
-  uint64_t tiles1, tiles2, sched, counters1, counters2, partials1, partials2;
+  int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
+  uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2;
 };
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
@@ -90,7 +90,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   const int bn_auto = pick_bn(T, E_l);
   P->bn1 = g_bn_override[0] ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
   P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_auto;
-  P->grid = sm_count;
+
   auto max_mt = [&](int bn) {
     long v = (long)P->R_cap / bn + E_l;
     return (int)(v < P->R_cap ? v : P->R_cap);
@@ -113,14 +113,17 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->sched = take(64);
   P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
+  P->ready = take((uint64_t)E_l * 4);
   P->pub.row_token = take(R * 4);
   P->pub.act = take(R * kHidden);
   P->pub.act_scale = take(R * kHiddenBlocks * 4);
   P->pub.inter = take(2 * R * kInter);
   P->pub.inter_scale = take(R * kInterBlocks * 4);
   P->pub.down = take(R * kHidden * 4);
-  P->partials1 = take(gemm_partials_bytes(1, P->bn1, P->grid));
-  P->partials2 = take(gemm_partials_bytes(2, P->bn2, P->grid));
+  P->grid1 = sm_count * gemm_ctas_per_sm(1, P->bn1);   // persistent: every resident CTA slot
+  P->grid2 = sm_count * gemm_ctas_per_sm(2, P->bn2);
+  P->partials1 = take(gemm_partials_bytes(1, P->bn1, P->grid1));
+  P->partials2 = take(gemm_partials_bytes(2, P->bn2, P->grid2));
   P->pub.total_bytes = off;
   P->pub.row_capacity = P->R_cap;
 }
@@ -192,6 +195,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   int32_t* sched = reinterpret_cast<int32_t*>(at(P.sched));
   int32_t* cnt1 = reinterpret_cast<int32_t*>(at(P.counters1));
   int32_t* cnt2 = reinterpret_cast<int32_t*>(at(P.counters2));
+  int* ready = reinterpret_cast<int*>(at(P.ready));
   int32_t* row_token = reinterpret_cast<int32_t*>(at(P.pub.row_token));
   uint8_t* inter = at(P.pub.inter);
   float* inter_scale = reinterpret_cast<float*>(at(P.pub.inter_scale));
@@ -213,7 +217,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     ce = launch_front(a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
                       a->local_expert_offset, E_l, P.R_cap, P.bn1, P.bn2, kInter / 128, kHidden / 128,
                       a->hidden_states, a->hidden_states_scale, ids, wts, masks8, P.NB8, seg, tiles1, tiles2,
-                      sched, cnt1, cnt2, inv, row_token, act, act_scale, err, s);
+                      sched, cnt1, cnt2, ready, inv, row_token, act, act_scale, err, s);
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(1, s);
     mark_stage(2, s);
@@ -224,7 +228,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(1, s);
     ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
-                     kInter / 128, cnt2, kHidden / 128, s);
+                     kInter / 128, cnt2, kHidden / 128, ready, s);
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
@@ -235,19 +239,21 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   GemmParams g1{};
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
   g1.b_scale = act_scale;
-  g1.counters = cnt1; g1.partials = reinterpret_cast<float*>(at(P.partials1));
+  g1.counters = cnt1; g1.ready = ready; g1.seg = seg; g1.bn_prev = 0;
+  g1.early_start = T <= kFrontMaxTokens ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
-  ce = launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid, s);
+  ce = launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   GemmParams g2{};
   g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale;
   g2.b_scale = inter_scale;
-  g2.counters = cnt2; g2.partials = reinterpret_cast<float*>(at(P.partials2));
+  g2.counters = cnt2; g2.ready = ready; g2.seg = seg; g2.bn_prev = P.bn1;
+  g2.early_start = T <= kFrontMaxTokens ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
-  ce = launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid, s);
+  ce = launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   mark_stage(5, s);

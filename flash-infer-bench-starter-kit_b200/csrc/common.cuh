@@ -78,6 +78,30 @@ __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- cross-CTA flags -------------------------------------------------------
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Order this thread's earlier (generic-proxy) observations before its later
+// async-proxy (TMA) accesses.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async;" ::: "memory");
+}
+// Spin (bounded) until *ctr >= target; false on timeout or when another role
+// has aborted.
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  while (ld_acquire_gpu(ctr) < target) {
+    if (*abort_flag) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) { *abort_flag = 1; return false; }
+    __nanosleep(128);
+  }
+  return true;
+}
+
 // ---- mbarrier -------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

@@ -46,7 +46,15 @@
 
 namespace moe {
 
-template <int KIND, int BN, int STAGES, int NWG, int KS>
+#ifdef MOE_GEMM_TIMELINE
+// Diagnostics builds only: per-CTA %globaltimer stamps of pipeline milestones.
+__device__ unsigned long long g_timeline[2][1024][8];
+#define MOE_TL(ev) g_timeline[KIND - 1][blockIdx.x][ev] = globaltimer_ns()
+#else
+#define MOE_TL(ev) ((void)0)
+#endif
+
+template <int KIND, int BN, int STAGES, int NWG, int KS, int OCC = 1>
 struct GemmCfg {
   static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles per K block
   static constexpr int MMA_N = KIND == 1 ? BN : 2 * BN;     // token-operand rows
@@ -74,7 +82,8 @@ struct GemmCfg {
   static_assert(CPW % 16 == 0 || (KIND == 2 && CPW % 8 == 0), "column chunking");
   static_assert(MMA_N % 16 == 0 && MMA_N <= 256, "MMA N");
   static_assert(SLOT <= NEPI, "one coefficient per epilogue thread");
-  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(SMEM * OCC <= 228 * 1024 - OCC * 1024, "shared memory budget");
+  static_assert(TMEM_COLS * OCC <= 512, "TMEM budget per SM");
 };
 
 struct Schedule {
@@ -92,11 +101,11 @@ __device__ __forceinline__ Schedule make_schedule(int n_mt, int NT, int KSTEPS) 
   return s;
 }
 
-template <int KIND, int BN, int STAGES, int NWG, int KS>
-__global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG, KS>::THREADS, 1)
+template <int KIND, int BN, int STAGES, int NWG, int KS, int OCC>
+__global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG, KS, OCC>::THREADS, OCC)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
                 const GemmParams p) {
-  using C = GemmCfg<KIND, BN, STAGES, NWG, KS>;
+  using C = GemmCfg<KIND, BN, STAGES, NWG, KS, OCC>;
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte alignment for 128-byte-swizzled TMA tiles.
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -115,7 +124,12 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  griddep_wait();                   // routing/permutation (or GEMM1) results are visible
+  if (threadIdx.x == 0) MOE_TL(0);
+  // GEMM1 waits for the routing/permutation kernels.  GEMM2 does not wait
+  // for GEMM1 as a whole: it starts streaming its weights on SMs GEMM1 has
+  // released and waits per expert (p.ready) before reading the intermediate.
+  if (KIND == 1 || !p.early_start) griddep_wait();
+  if (threadIdx.x == 0) MOE_TL(1);
   griddep_launch_dependents();
   const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KSTEPS);
   if (sch.it0 >= sch.it1) return;   // uniform: this CTA has no work
@@ -141,6 +155,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_b = l2_policy_evict_last();
       int issued = 0;
+      int ready_e = -1;                 // GEMM2: expert whose intermediate is known complete
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
         const int it = sch.it0 + i;
@@ -155,6 +170,13 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         const int wrow = tile.x * C::W_ROWS + nt * 128;
         tma_load_3d(&tm_w, &full[s], st, 0, wrow, z, pol_w);
         if (KIND == 1) tma_load_3d(&tm_w, &full[s], st + KS * C::W_TILE, 0, wrow + kInter, z, pol_w);
+        if (KIND == 2 && p.early_start && tile.x != ready_e) {
+          const int cnt = p.seg[tile.x + 1] - p.seg[tile.x];
+          const int target = (kInter / 128) * ((cnt + p.bn_prev - 1) / p.bn_prev);
+          if (!wait_counter(p.ready + tile.x, target, abort_flag)) { ok = false; ++issued; break; }
+          fence_proxy_async();
+          ready_e = tile.x;
+        }
         tma_load_3d(&tm_b, &full[s], st + C::NW * KS * C::W_TILE, 0,
                     KIND == 1 ? tile.y : 2 * tile.y, z, pol_b);
         ++issued;
@@ -178,6 +200,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       for (int i = 0; i < n_iter; ++i) {
         const int s = i % STAGES, b = i % C::NBUF;
         if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
+        if (i == 0) MOE_TL(2);
         if (!mbar_wait_bounded(&tempty[b], ((i / C::NBUF) & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = smem_base + s * C::STAGE;
@@ -196,6 +219,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         tc_commit(&empty[s]);
         tc_commit(&tfull[b]);
       }
+      MOE_TL(3);
       if (!ok) raise_error(p.err, kDevTimeoutMma);
       // Wait for every MMA this thread issued before TMEM is released.
       tc_commit(drain);
@@ -233,11 +257,16 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         pf_e = tl.x;
         pf_nt = u_t / sch.n_mt;
         pf_col = my_j < tl.z ? tl.y + my_j : -1;
+        if (KIND == 2 && p.early_start && pf_col >= 0) {   // the intermediate's scales come from GEMM1
+          const int cnt = p.seg[pf_e + 1] - p.seg[pf_e];
+          wait_counter(p.ready + pf_e, (kInter / 128) * ((cnt + p.bn_prev - 1) / p.bn_prev), abort_flag);
+        }
       }
       if (pf_col < 0) return 0.f;
       const int nb = KIND == 1 ? pf_nt + my_w * (kInter / 128) : pf_nt;
       const float wsc = __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
-      return wsc * __ldg(p.b_scale + (size_t)kb_t * p.R_cap + pf_col);
+      const float* bs = p.b_scale + (size_t)kb_t * p.R_cap + pf_col;
+      return wsc * ((KIND == 2 && p.early_start) ? __ldcg(bs) : __ldg(bs));
     };
     for (int i_t = 0; i_t < 2 && i_t < n_iter; ++i_t)
       if (loader) sring[i_t * C::SLOT + et] = fetch(i_t);
@@ -324,6 +353,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (*abort_flag) break;
 
       const bool seg_last = (ks == C::KSTEPS - 1) || (it == sch.it1 - 1);
+      if (et == 0 && i == n_iter - 1) MOE_TL(6);
       if (!seg_last) continue;
 
       // ---------------- end of this CTA's share of unit u
@@ -346,20 +376,40 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
         }
         named_bar_sync(1, C::NEPI);
+        if (et == 0 && i == n_iter - 1) MOE_TL(7);
         if (!last_flag[0]) continue;
         __threadfence();
-#pragma unroll
-        for (int w = 0; w < C::NW; ++w)
-#pragma unroll
-          for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
-        for (int c = c_lo; c <= c_hi; ++c) {
+        if (c_hi - c_lo == 1) {
+          // Two contributors: fp32 addition is commutative, so adding the other
+          // CTA's partial to our registers is the same sum whoever is last.
+          const int c = (c_lo == (int)blockIdx.x) ? c_hi : c_lo;
           const int cslot = (u == (c * sch.L) / C::KSTEPS) ? 0 : 1;
           const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
+          float other[C::NW][C::CPW];
 #pragma unroll
           for (int w = 0; w < C::NW; ++w)
 #pragma unroll
             for (int jj = 0; jj < C::CPW; ++jj)
-              acc[w][jj] += __ldcg(src + ((size_t)w * BN + j0 + jj) * 128 + f);
+              other[w][jj] = __ldcg(src + ((size_t)w * BN + j0 + jj) * 128 + f);
+#pragma unroll
+          for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+            for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] += other[w][jj];
+        } else {
+          // Three or more: sum every published partial in ascending CTA order.
+#pragma unroll
+          for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+            for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
+          for (int c = c_lo; c <= c_hi; ++c) {
+            const int cslot = (u == (c * sch.L) / C::KSTEPS) ? 0 : 1;
+            const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
+#pragma unroll
+            for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+              for (int jj = 0; jj < C::CPW; ++jj)
+                acc[w][jj] += __ldcg(src + ((size_t)w * BN + j0 + jj) * 128 + f);
+          }
         }
       }
       if (KIND == 1) {
@@ -368,7 +418,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
         for (int jj = 0; jj < C::CPW; ++jj) {
           const float x1 = acc[0][jj], x2 = acc[C::NW - 1][jj];
-          const float cv = __fmul_rn(__fdiv_rn(x2, __fadd_rn(1.0f, expf(-x2))), x1);
+          const float cv = x2 * __frcp_rn(1.0f + __expf(-x2)) * x1;
           acc[0][jj] = cv;
           float m = fabsf(cv);
 #pragma unroll
@@ -380,7 +430,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         for (int jj = 0; jj < C::CPW; ++jj) {
           const float* am = samax + wg * 4 * C::CPW + jj;
           const float amax = fmaxf(fmaxf(am[0], am[C::CPW]), fmaxf(am[2 * C::CPW], am[3 * C::CPW]));
-          const float s = amax > 0.f ? __fdiv_rn(amax, kFp8Max) : 1.0f;
+          const float s = amax > 0.f ? amax * (1.0f / kFp8Max) : 1.0f;
           const float inv = __frcp_rn(s);
           const float cv = acc[0][jj];
           const uint8_t hi = f32_to_e4m3(__fmul_rn(cv, inv));
@@ -394,7 +444,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             if (f == 0) p.inter_scale[(size_t)nt * p.R_cap + row] = s;
           }
         }
-        named_bar_sync(2 + wg, 128);
+        if (p.early_start) {
+          // all warpgroups' stores of this unit, then one release increment
+          __threadfence();
+          named_bar_sync(1, C::NEPI);
+          if (et == 0) atomicAdd(p.ready + tile.x, 1);
+        } else {
+          named_bar_sync(2 + wg, 128);
+        }
       } else {
 #pragma unroll
         for (int jj = 0; jj < C::CPW; ++jj) {
@@ -404,11 +461,13 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
     }
+    if (et == 0) MOE_TL(4);
     if (*abort_flag) raise_error(p.err, kDevTimeoutEpilogue);
   }
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) MOE_TL(5);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -420,24 +479,24 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 // Host-side dispatch: (kind, BN) -> stages, warpgroups, K blocks per stage.
 // --------------------------------------------------------------------------
 template <int KIND, int BN> struct Pick;
-template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2; };
-template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2; };
-template <> struct Pick<1, 64> { static constexpr int S = 5, W = 2, K = 1; };
-template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1; };
-template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2; };
-template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2; };
-template <> struct Pick<2, 64> { static constexpr int S = 6, W = 1, K = 1; };
-template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1; };
+template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
+template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
+template <> struct Pick<1, 64> { static constexpr int S = 5, W = 2, K = 1, O = 1; };
+template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
+template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2, O = 1; };
+template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2, O = 1; };
+template <> struct Pick<2, 64> { static constexpr int S = 6, W = 1, K = 1, O = 1; };
+template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
 
 template <int KIND, int BN>
-using CfgOf = GemmCfg<KIND, BN, Pick<KIND, BN>::S, Pick<KIND, BN>::W, Pick<KIND, BN>::K>;
+using CfgOf = GemmCfg<KIND, BN, Pick<KIND, BN>::S, Pick<KIND, BN>::W, Pick<KIND, BN>::K, Pick<KIND, BN>::O>;
 
 template <int KIND, int BN>
 static cudaError_t launch_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
                               int grid, cudaStream_t st) {
   using P = Pick<KIND, BN>;
   using C = CfgOf<KIND, BN>;
-  auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W, P::K>;
+  auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W, P::K, P::O>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
@@ -461,6 +520,14 @@ int gemm_k_per_stage(int kind, int bn) {
   return 0;
 }
 
+int gemm_ctas_per_sm(int kind, int bn) {
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return Pick<KD, BB>::O;
+  MOE_GEMM_CASES(X)
+#undef X
+  return 1;
+}
+
 int gemm_threads(int kind, int bn) {
 #define X(KD, BB) \
   if (kind == KD && bn == BB) return CfgOf<KD, BB>::THREADS;
@@ -479,3 +546,9 @@ cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtenso
 }
 
 }  // namespace moe
+
+#ifdef MOE_GEMM_TIMELINE
+extern "C" __attribute__((visibility("default"))) int moe_probe_timeline(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, moe::g_timeline, sizeof(moe::g_timeline)) == cudaSuccess ? 0 : 1;
+}
+#endif

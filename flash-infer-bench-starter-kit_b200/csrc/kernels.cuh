@@ -12,6 +12,10 @@ struct GemmParams {
   const float* w_scale;       // GEMM1: [E_l, 32, 56]; GEMM2: [E_l, 56, 16]
   const float* b_scale;       // GEMM1: act_scale [56, R_cap]; GEMM2: inter_scale [16, R_cap]
   int32_t* counters;          // stream-K arrival counters, one per output tile
+  int* ready;                 // per local expert: GEMM1 units finished (GEMM1 adds, GEMM2 waits)
+  const int32_t* seg;         // per-expert row offsets (GEMM2: rows of expert e)
+  int bn_prev;                // GEMM2: GEMM1's token-tile width
+  int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048]
   float* inter_scale;         // GEMM1 output: [16, R_cap]
@@ -27,6 +31,7 @@ constexpr int kBnConfigs[kNumBnConfigs] = {16, 32, 64, 128};
 size_t gemm_partials_bytes(int kind, int bn, int grid);
 int gemm_threads(int kind, int bn);
 int gemm_k_per_stage(int kind, int bn);
+int gemm_ctas_per_sm(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st);
 
@@ -35,7 +40,8 @@ cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, i
                          uint8_t* masks8, int NB8p, int* err, cudaStream_t st);
 cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
-                        int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st);
+                        int32_t* counters1, int nt1, int32_t* counters2, int nt2, int* ready,
+                        cudaStream_t st);
 cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
@@ -45,7 +51,7 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
                          int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2, const void* hidden,
                          const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
                          int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
-                         int32_t* counters1, int32_t* counters2, int32_t* inv_row,
+                         int32_t* counters1, int32_t* counters2, int* ready, int32_t* inv_row,
                          int32_t* row_token, uint8_t* act, float* act_scale, int* err,
                          cudaStream_t st);
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,

@@ -11,6 +11,14 @@
 
 namespace moe {
 
+#ifdef MOE_GEMM_TIMELINE
+// Diagnostics builds only: per-CTA %globaltimer stamps of the front end.
+__device__ unsigned long long g_front_timeline[64][8];
+#define MOE_FTL(ev) if (threadIdx.x == 0) g_front_timeline[blockIdx.x & 63][ev] = globaltimer_ns()
+#else
+#define MOE_FTL(ev) ((void)0)
+#endif
+
 // --------------------------------------------------------------------------
 // Routing + per-block token masks of local experts.
 //
@@ -50,7 +58,11 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
     float s[8], sb[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
+#ifdef MOE_ROUTE_EXPF_PROBE
+      float e = expf(-x[j]);
+#else
       float e = (float)exp(-(double)x[j]);
+#endif
       s[j] = __frcp_rn(__fadd_rn(1.0f, e));
       sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
     }
@@ -242,7 +254,7 @@ scan_kernel(const uint8_t* __restrict__ masks8, int NB8p, int32_t* __restrict__ 
             int32_t* __restrict__ seg_out,
             int bn1, int bn2, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
             int32_t* __restrict__ sched, int32_t* __restrict__ counters1, int nt1,
-            int32_t* __restrict__ counters2, int nt2) {
+            int32_t* __restrict__ counters2, int nt2, int* __restrict__ ready) {
   __shared__ int s_cnt[kExpertsGlobal];
   __shared__ int s_seg[kExpertsGlobal + 1];
   __shared__ int s_t1[kExpertsGlobal];
@@ -302,6 +314,7 @@ scan_kernel(const uint8_t* __restrict__ masks8, int NB8p, int32_t* __restrict__ 
   const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
   for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
   for (int i = threadIdx.x; i < units2; i += blockDim.x) counters2[i] = 0;
+  for (int e = threadIdx.x; e < E_l; e += blockDim.x) ready[e] = 0;
   if (threadIdx.x == 0) {
     sched[0] = s_tot[1];
     sched[1] = s_tot[2];
@@ -413,7 +426,7 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
              int32_t* __restrict__ topk_ids, float* __restrict__ topk_w, uint8_t* __restrict__ masks8,
              int NB8p, int32_t* __restrict__ seg_out, int4* __restrict__ tiles1, int4* __restrict__ tiles2,
              int32_t* __restrict__ sched, int32_t* __restrict__ counters1,
-             int32_t* __restrict__ counters2, int32_t* __restrict__ inv_row,
+             int32_t* __restrict__ counters2, int* __restrict__ ready, int32_t* __restrict__ inv_row,
              int32_t* __restrict__ row_token, uint8_t* __restrict__ act, float* __restrict__ act_scale,
              int* __restrict__ err) {
   __shared__ uint32_t s_mask[kExpertsGlobal];
@@ -425,7 +438,9 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   __shared__ int s_n;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
+  MOE_FTL(0);
   griddep_wait();
+  MOE_FTL(1);
   griddep_launch_dependents();
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
   if (threadIdx.x == 0) s_n = 0;
@@ -442,7 +457,9 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   }
   __syncthreads();
   store_masks(masks8, NB8p, E_l, s_mask);
+  MOE_FTL(2);
   if (!grid_barrier(err + 1, err + 2, err)) return;
+  MOE_FTL(3);
   // ---- phase 2: per-expert counts and this CTA's first row per expert
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
     const unsigned int* row = reinterpret_cast<const unsigned int*>(masks8 + (size_t)e * NB8p);
@@ -489,8 +506,10 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
     for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
     for (int i = threadIdx.x; i < units2; i += blockDim.x) counters2[i] = 0;
+    for (int e = threadIdx.x; e < E_l; e += blockDim.x) ready[e] = 0;
     if (threadIdx.x == 0) { sched[0] = s_tot[1]; sched[1] = s_tot[2]; sched[2] = s_tot[0]; }
   }
+  MOE_FTL(4);
   // ---- phase 3: rows of own tokens, inverse map, activation gather
   if (threadIdx.x < kRouteTokens * kTopK) {
     const int w8 = threadIdx.x / kTopK, k = threadIdx.x % kTopK;
@@ -535,6 +554,8 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     const int kb = v % kHiddenBlocks;
     act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
   }
+  __syncthreads();
+  MOE_FTL(5);
 }
 
 // --------------------------------------------------------------------------
@@ -600,9 +621,10 @@ cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, i
 
 cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB, int E_l, int32_t* seg,
                         int bn1, int bn2, int4* tiles1, int4* tiles2, int32_t* sched,
-                        int32_t* counters1, int nt1, int32_t* counters2, int nt2, cudaStream_t st) {
+                        int32_t* counters1, int nt1, int32_t* counters2, int nt2, int* ready,
+                        cudaStream_t st) {
   return launch_pdl(scan_kernel, dim3(1), dim3(1024), 0, st, masks8, NB8p, bases, NB, E_l, seg, bn1, bn2,
-                    tiles1, tiles2, sched, counters1, nt1, counters2, nt2);
+                    tiles1, tiles2, sched, counters1, nt1, counters2, nt2, ready);
 }
 
 cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
@@ -620,7 +642,7 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
                          int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2, const void* hidden,
                          const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
                          int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
-                         int32_t* counters1, int32_t* counters2, int32_t* inv_row,
+                         int32_t* counters1, int32_t* counters2, int* ready, int32_t* inv_row,
                          int32_t* row_token, uint8_t* act, float* act_scale, int* err,
                          cudaStream_t st) {
   const int nb = (T + kRouteTokens - 1) / kRouteTokens;
@@ -628,7 +650,7 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
   return launch_pdl(front_kernel, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits,
                     static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, R_cap, bn1,
                     bn2, nt1, nt2, static_cast<const uint8_t*>(hidden), hs_scale, ids, w, masks8, NB8p, seg,
-                    tiles1, tiles2, sched, counters1, counters2, inv_row, row_token, act, act_scale, err);
+                    tiles1, tiles2, sched, counters1, counters2, ready, inv_row, row_token, act, act_scale, err);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
@@ -639,3 +661,9 @@ cudaError_t launch_combine(const float* down, const int32_t* inv_row, const floa
 }
 
 }  // namespace moe
+
+#ifdef MOE_GEMM_TIMELINE
+extern "C" __attribute__((visibility("default"))) int moe_probe_front_timeline(unsigned long long* host) {
+  return cudaMemcpyFromSymbol(host, moe::g_front_timeline, sizeof(moe::g_front_timeline)) == cudaSuccess ? 0 : 1;
+}
+#endif
