@@ -296,43 +296,33 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           for (int w = 0; w < C::NW; ++w) {
             const float* coef = sl + (kk * C::NW + w) * BN + j0;
             const uint32_t col0 = (uint32_t)(b * C::BUF_COLS + (kk * C::NW + w) * C::MMA_N);
-            if (KIND == 1) {
-              // 16 token columns per TMEM load, two loads in flight per wait
+            // TMEM columns of this warpgroup: KIND 1 one per token, KIND 2 two
+            // per token (hi, lo).  Loads of LDC columns, two in flight per wait.
+            constexpr int TCOLS = KIND == 1 ? C::CPW : 2 * C::CPW;
+            constexpr int LDC = 16;
+            constexpr int NLD = TCOLS / LDC;
+            const uint32_t tcol = col0 + (KIND == 1 ? j0 : 2 * j0);
 #pragma unroll
-              for (int c = 0; c < C::CPW / 16; c += 2) {
-                float v[2][16];
-                tmem_ld16(tmem_base + lane_addr + col0 + j0 + c * 16, v[0]);
-                if (c + 1 < C::CPW / 16) tmem_ld16(tmem_base + lane_addr + col0 + j0 + (c + 1) * 16, v[1]);
-                tmem_ld_wait();
+            for (int c = 0; c < NLD; c += 2) {
+              float v[2][LDC];
+              tmem_ld<LDC>(tmem_base + lane_addr + tcol + c * LDC, v[0]);
+              if (c + 1 < NLD) tmem_ld<LDC>(tmem_base + lane_addr + tcol + (c + 1) * LDC, v[1]);
+              tmem_ld_wait();
 #pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  if (c + h >= C::CPW / 16) break;
+              for (int h = 0; h < 2; ++h) {
+                if (c + h >= NLD) break;
+                constexpr int TOK = KIND == 1 ? LDC : LDC / 2;     // token columns per load
 #pragma unroll
-                  for (int x4 = 0; x4 < 4; ++x4) {
-                    const float4 cf = reinterpret_cast<const float4*>(coef + (c + h) * 16)[x4];
-                    const int jj = (c + h) * 16 + x4 * 4;
-                    acc[w][jj + 0] = fmaf(v[h][x4 * 4 + 0], cf.x, acc[w][jj + 0]);
-                    acc[w][jj + 1] = fmaf(v[h][x4 * 4 + 1], cf.y, acc[w][jj + 1]);
-                    acc[w][jj + 2] = fmaf(v[h][x4 * 4 + 2], cf.z, acc[w][jj + 2]);
-                    acc[w][jj + 3] = fmaf(v[h][x4 * 4 + 3], cf.w, acc[w][jj + 3]);
-                  }
-                }
-              }
-            } else {
-              // TMEM columns (2j, 2j+1) = (hi, lo) of token j: 8 tokens per load
-#pragma unroll
-              for (int c = 0; c < C::CPW / 8; c += 2) {
-                float v[2][16];
-                tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + c * 16, v[0]);
-                if (c + 1 < C::CPW / 8) tmem_ld16(tmem_base + lane_addr + col0 + 2 * j0 + (c + 1) * 16, v[1]);
-                tmem_ld_wait();
-#pragma unroll
-                for (int h = 0; h < 2; ++h) {
-                  if (c + h >= C::CPW / 8) break;
-#pragma unroll
-                  for (int x4 = 0; x4 < 2; ++x4) {
-                    const float4 cf = reinterpret_cast<const float4*>(coef + (c + h) * 8)[x4];
-                    const int jj = (c + h) * 8 + x4 * 4;
+                for (int x4 = 0; x4 < TOK / 4; ++x4) {
+                  const float4 cf = reinterpret_cast<const float4*>(coef + (c + h) * TOK)[x4];
+                  const int jj = (c + h) * TOK + x4 * 4;
+                  if (KIND == 1) {
+                    const float* vv = v[h] + x4 * 4;
+                    acc[w][jj + 0] = fmaf(vv[0], cf.x, acc[w][jj + 0]);
+                    acc[w][jj + 1] = fmaf(vv[1], cf.y, acc[w][jj + 1]);
+                    acc[w][jj + 2] = fmaf(vv[2], cf.z, acc[w][jj + 2]);
+                    acc[w][jj + 3] = fmaf(vv[3], cf.w, acc[w][jj + 3]);
+                  } else {
                     const float* vv = v[h] + x4 * 8;
                     acc[w][jj + 0] = fmaf(fmaf(vv[1], 0.0625f, vv[0]), cf.x, acc[w][jj + 0]);
                     acc[w][jj + 1] = fmaf(fmaf(vv[3], 0.0625f, vv[2]), cf.y, acc[w][jj + 1]);
@@ -349,8 +339,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
       if (loader && i + 2 < n_iter) sring[((i + 2) % C::RING) * C::SLOT + et] = pre;
-      named_bar_sync(1, C::NEPI);
-      if (*abort_flag) break;
+      if (named_bar_or(1, C::NEPI, *abort_flag != 0)) break;   // uniform abort decision
 
       const bool seg_last = (ks == C::KSTEPS - 1) || (it == sch.it1 - 1);
       if (et == 0 && i == n_iter - 1) MOE_TL(6);
