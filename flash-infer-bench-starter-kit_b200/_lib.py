@@ -51,7 +51,7 @@ class MoeLayout(ctypes.Structure):
     """struct moe_fp8_ds_layout."""
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "total_bytes", "error_word", "topk_ids", "topk_weights", "inv_row", "seg_offsets",
-        "row_token", "block_masks", "block_bases", "inter", "inter_scale", "down", "act", "act_scale")] + [
+        "row_token", "block_masks", "block_bases", "inter", "inter_scale", "down", "act", "act_scale", "act16", "inter16")] + [
         ("row_capacity", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
@@ -59,7 +59,7 @@ EXPORTS = (
     "moe_fp8_ds_workspace_size", "moe_fp8_ds_workspace_layout", "moe_fp8_ds_run",
     "moe_fp8_ds_run_routed", "moe_fp8_ds_route", "moe_fp8_ds_read_device_error",
     "moe_fp8_ds_status_string", "moe_fp8_ds_launches_per_call", "moe_fp8_ds_set_tile_override",
-    "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc",
+    "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc", "moe_fp8_ds_set_path_override",
 )
 
 _lib = None
@@ -89,6 +89,7 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_run.argtypes = [ctypes.POINTER(MoeArgs), P, U64, P]
         lib.moe_fp8_ds_run_routed.argtypes = [ctypes.POINTER(MoeArgs), P, U64, P]
         lib.moe_fp8_ds_run_noalloc.argtypes = [ctypes.POINTER(MoeArgs), P]
+        lib.moe_fp8_ds_set_path_override.argtypes = [I32]
         lib.moe_fp8_ds_route.argtypes = [P, P, I32, ctypes.c_float, P, P, P]
         lib.moe_fp8_ds_read_device_error.argtypes = [P, P, ctypes.POINTER(I32)]
         lib.moe_fp8_ds_status_string.argtypes = [ctypes.c_int]

@@ -29,6 +29,8 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
+int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
+constexpr int kWideMinTokens = 4096;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -73,6 +75,7 @@ int pick_bn(int T, int E_l) {
 struct Plan {
   moe_fp8_ds_layout pub;
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
+  bool wide;                        // large batch: f16-operand GEMMs (gemm_f16.cu)
   uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2;
 };
 
@@ -88,8 +91,19 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  P->bn1 = g_bn_override[0] ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
-  P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_auto;
+  // f16-operand GEMMs win once experts see ~128 tokens each (measured on B200:
+  // equal at T=4096, 25% faster at T=8192, slower below).
+  P->wide = g_path_override == 2 || (g_path_override == 0 && T >= kWideMinTokens);
+  if (P->wide) {
+    // f16 kernels accumulate in TMEM, so tiles are as wide as TMEM allows:
+    // GEMM1 up to 128 tokens (X1 and X2), GEMM2 up to 256.
+    const double per_expert = (double)T * kTopK / kExpertsGlobal;
+    P->bn1 = per_expert > 64.0 ? 128 : 64;
+    P->bn2 = per_expert > 128.0 ? 256 : per_expert > 64.0 ? 128 : 64;
+  } else {
+    P->bn1 = g_bn_override[0] ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
+    P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_auto;
+  }
 
   auto max_mt = [&](int bn) {
     long v = (long)P->R_cap / bn + E_l;
@@ -115,15 +129,24 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->ready = take((uint64_t)E_l * 4);
   P->pub.row_token = take(R * 4);
-  P->pub.act = take(R * kHidden);
-  P->pub.act_scale = take(R * kHiddenBlocks * 4);
-  P->pub.inter = take(2 * R * kInter);
-  P->pub.inter_scale = take(R * kInterBlocks * 4);
+  const uint64_t R8 = P->wide ? 0 : R, R16 = P->wide ? R : 0;   // only the active path's buffers
+  P->pub.act = take(R8 * kHidden);
+  P->pub.act_scale = take(R8 * kHiddenBlocks * 4);
+  P->pub.inter = take(2 * R8 * kInter);
+  P->pub.inter_scale = take(R8 * kInterBlocks * 4);
+  P->pub.act16 = take(R16 * kHidden * 2);
+  P->pub.inter16 = take(R16 * kInter * 2);
   P->pub.down = take(R * kHidden * 4);
-  P->grid1 = sm_count * gemm_ctas_per_sm(1, P->bn1);   // persistent: every resident CTA slot
-  P->grid2 = sm_count * gemm_ctas_per_sm(2, P->bn2);
-  P->partials1 = take(gemm_partials_bytes(1, P->bn1, P->grid1));
-  P->partials2 = take(gemm_partials_bytes(2, P->bn2, P->grid2));
+  if (P->wide) {
+    P->grid1 = P->grid2 = sm_count;
+    P->partials1 = take(gemm_f16_partials_bytes(1, P->bn1, P->grid1));
+    P->partials2 = take(gemm_f16_partials_bytes(2, P->bn2, P->grid2));
+  } else {
+    P->grid1 = sm_count * gemm_ctas_per_sm(1, P->bn1);   // persistent: every resident CTA slot
+    P->grid2 = sm_count * gemm_ctas_per_sm(2, P->bn2);
+    P->partials1 = take(gemm_partials_bytes(1, P->bn1, P->grid1));
+    P->partials2 = take(gemm_partials_bytes(2, P->bn2, P->grid2));
+  }
   P->pub.total_bytes = off;
   P->pub.row_capacity = P->R_cap;
 }
@@ -141,6 +164,30 @@ bool encode_kmajor(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, 
                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
+}
+
+// e4m3 weights [rows, K] as {x = byte inside a 64-byte K atom, atom, row};
+// box = 64 bytes x 1 atom x 128 rows, unswizzled (converter staging).
+bool encode_w8_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
+  cuuint64_t dims[3] = {64, K / 64, rows};
+  cuuint64_t strides[2] = {64, K};
+  cuuint32_t box[3] = {64, 1, 128};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// f16 tokens [rows, K] as {x = element inside a 64-element K atom, atom, row};
+// box = 64 elements x 1 atom x box_rows rows with 128-byte swizzle.
+bool encode_b16_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
+  cuuint64_t dims[3] = {64, K / 64, rows};
+  cuuint64_t strides[2] = {128, K * 2};
+  cuuint32_t box[3] = {64, 1, box_rows};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
+                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -202,16 +249,26 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   float* down = reinterpret_cast<float*>(at(P.pub.down));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
+  __half* act16 = reinterpret_cast<__half*>(at(P.pub.act16));
+  __half* inter16 = reinterpret_cast<__half*>(at(P.pub.inter16));
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
+  if (P.wide) {
+    if (!encode_w8_atoms(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out) ||
+        !encode_b16_atoms(&tm_b1, act16, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
+        !encode_w8_atoms(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden) ||
+        !encode_b16_atoms(&tm_b2, inter16, kInter, (uint64_t)P.R_cap, (uint32_t)P.bn2))
+      return MOE_ERR_INVALID_ARGUMENT;
+  } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
   if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
       !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1, ks1) ||
       !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
       !encode_kmajor(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2), ks2))
     return MOE_ERR_INVALID_ARGUMENT;
+  }
 
   cudaError_t ce;
-  if (!routed && T <= kFrontMaxTokens) {
+  if (!routed && T <= kFrontMaxTokens && !P.wide) {
     // Small batch: routing, row assignment and gather in one launch.
     mark_stage(0, s);
     ce = launch_front(a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
@@ -232,7 +289,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
-                        a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale, s);
+                        a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale,
+                        P.wide ? act16 : nullptr, s);
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
   }
 
@@ -240,20 +298,24 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
   g1.b_scale = act_scale;
   g1.counters = cnt1; g1.ready = ready; g1.seg = seg; g1.bn_prev = 0;
-  g1.early_start = T <= kFrontMaxTokens ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
+  g1.early_start = (!routed && T <= kFrontMaxTokens && !P.wide) ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
-  ce = launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
+  g1.inter16 = inter16;
+  ce = P.wide ? launch_gemm_f16(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s)
+              : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   GemmParams g2{};
   g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale;
   g2.b_scale = inter_scale;
   g2.counters = cnt2; g2.ready = ready; g2.seg = seg; g2.bn_prev = P.bn1;
-  g2.early_start = T <= kFrontMaxTokens ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
+  g2.early_start = (!routed && T <= kFrontMaxTokens && !P.wide) ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
-  ce = launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
+  g2.inter16 = nullptr;
+  ce = P.wide ? launch_gemm_f16(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s)
+              : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   mark_stage(5, s);
@@ -374,6 +436,13 @@ int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
     g_stage_events[i] = static_cast<cudaEvent_t>(events[i]);
   }
   g_stage_events_on = true;
+  return MOE_OK;
+}
+
+int moe_fp8_ds_set_path_override(int32_t mode) {
+  if (mode < 0 || mode > 2) return MOE_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_path_override = mode;
   return MOE_OK;
 }
 

@@ -1,0 +1,389 @@
+// Grouped GEMMs for large batches (T > 256 tokens): block scales folded into
+// f16 operands, whole-K accumulation in TMEM.
+//
+// The e4m3 GEMMs (gemm_fp8.cu) must promote every 128-wide K block from TMEM
+// into registers because the fp32 block scales cannot enter an fp8 MMA.  For
+// large token tiles that promotion costs more registers and issue slots than a
+// CTA has.  Here the scales are applied to the operands instead:
+//   * the token operand arrives in f16 with its 1x128 scales already applied
+//     (the scatter kernel writes it that way for GEMM1; GEMM1's epilogue writes
+//     the SwiGLU output in f16 for GEMM2);
+//   * the weight tile is loaded in e4m3 by TMA and converted to f16 with its
+//     128x128 block scale by four converter warps, straight into the 128-byte
+//     swizzled K-major layout the MMA reads;
+// and tcgen05.mma kind::f16 accumulates the whole K loop of a tile in TMEM, so
+// the epilogue runs once per tile.  f16 keeps 11 significant bits (relative
+// 2^-12 per operand; values here stay far inside its range); products
+// accumulate in fp32.
+//
+// Same "swap AB" orientation as the e4m3 kernels: MMA M = 128 weight rows,
+// N = BN tokens.  One pipeline stage is one 64-element K atom (128 bytes of
+// f16 per row).  GEMM1 (KIND 1) holds the X1 and X2 rows of 128 features, so
+// SwiGLU runs in the epilogue; GEMM2 (KIND 2) writes fp32 rows for the combine.
+// Scheduling is the persistent stream-K of the e4m3 kernels; a split tile's
+// partial sums are published to global memory and added, in fixed CTA order,
+// by the last contributor.
+//
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 weight
+// converters, 6-9 epilogue.
+#include "kernels.cuh"
+
+namespace moe {
+
+template <int KIND, int BN, int STAGES>
+struct B16Cfg {
+  static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles (X1, X2) per stage
+  static constexpr int K = KIND == 1 ? kHidden : kInter;    // reduction length
+  static constexpr int ATOMS = K / 64;                      // pipeline iterations per tile
+  static constexpr int NT = KIND == 1 ? kInter / 128 : kHidden / 128;
+  static constexpr int W_ROWS = KIND == 1 ? kGemm1Out : kHidden;
+  static constexpr int W8_TILE = 128 * 64;                  // e4m3 staging: 128 rows x 64 B
+  static constexpr int W16_TILE = 128 * 128;                // f16: 128 rows x 128 B (swizzled)
+  static constexpr int B_TILE = BN * 128;                   // f16 tokens: BN rows x 128 B
+  static constexpr int OFF_W16 = NW * W8_TILE;
+  static constexpr int OFF_B = OFF_W16 + NW * W16_TILE;
+  static constexpr int STAGE = OFF_B + B_TILE;
+  static constexpr int ACC = NW * BN;                       // TMEM columns of one tile accumulator
+  static constexpr int TMEM_COLS = 2 * ACC <= 128 ? 128 : 2 * ACC <= 256 ? 256 : 512;
+  static constexpr int THREADS = 320;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;
+  static_assert(STAGE % 1024 == 0, "1024-byte aligned stages");
+  static_assert(2 * ACC <= 512, "two TMEM accumulators");
+  static_assert(BN % 16 == 0 && BN <= 256, "MMA N");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+// Instruction descriptor for kind::f16: A = B = f16, D = f32, K-major, M = 128.
+__host__ __device__ constexpr uint32_t make_idesc_f16(int m, int n) {
+  return (1u << 4) | (0u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+struct B16Schedule {
+  int n_mt, units, total, L, it0, it1;
+};
+
+template <int KIND, int BN, int STAGES>
+__global__ void __launch_bounds__(320, 1)
+moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
+                     const GemmParams p) {
+  using C = B16Cfg<KIND, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* aux = smem + STAGES * C::STAGE;
+  uint64_t* full = reinterpret_cast<uint64_t*>(aux);       // TMA bytes of stage s landed
+  uint64_t* conv = full + STAGES;                           // converters wrote stage s
+  uint64_t* empty = conv + STAGES;                          // MMA finished with stage s
+  uint64_t* accf = empty + STAGES;                          // accumulator b complete
+  uint64_t* acce = accf + 2;                                // accumulator b drained
+  uint64_t* drain = acce + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  griddep_wait();
+  griddep_launch_dependents();
+  B16Schedule sch;
+  sch.n_mt = p.sched[KIND - 1];
+  sch.units = sch.n_mt * C::NT;
+  sch.total = sch.units * C::ATOMS;
+  sch.L = (sch.total + gridDim.x - 1) / gridDim.x;
+  sch.it0 = min(sch.total, (int)blockIdx.x * sch.L);
+  sch.it1 = min(sch.total, sch.it0 + sch.L);
+  if (sch.it0 >= sch.it1) return;
+  const int n_iter = sch.it1 - sch.it0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
+    mbar_init(drain, 1);
+    *const_cast<int*>(abort_flag) = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tm_w); tma_prefetch_desc(&tm_b); }
+  if (warp == 1) tmem_alloc(tmem_slot, C::TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one_lane()) {
+      const uint64_t pol_w = l2_policy_evict_first();
+      const uint64_t pol_b = l2_policy_evict_last();
+      int issued = 0;
+      bool ok = true;
+      for (int i = 0; i < n_iter; ++i) {
+        const int it = sch.it0 + i;
+        const int u = it / C::ATOMS, a = it % C::ATOMS;
+        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+        const int4 tile = p.tiles[mt];
+        const int s = i % STAGES;
+        if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], C::NW * C::W8_TILE + C::B_TILE);
+        uint8_t* st = smem + s * C::STAGE;
+        // weights: e4m3 [rows][64 B] per tile (X1 then X2 for GEMM1)
+        tma_load_3d(&tm_w, &full[s], st, 0, a, tile.x * C::W_ROWS + nt * 128, pol_w);
+        if (KIND == 1)
+          tma_load_3d(&tm_w, &full[s], st + C::W8_TILE, 0, a, tile.x * C::W_ROWS + kInter + nt * 128, pol_w);
+        // tokens: f16 [BN rows][64 elements], 128-byte swizzle
+        tma_load_3d(&tm_b, &full[s], st + C::OFF_B, 0, a, tile.y, pol_b);
+        ++issued;
+      }
+      if (!ok) {
+        raise_error(p.err, kDevTimeoutProducer);
+        for (int i = max(0, issued - STAGES); i < issued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+                 globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one_lane()) {
+      constexpr uint32_t idesc = make_idesc_f16(128, BN);
+      const uint32_t smem_base = smem_u32(smem);
+      bool ok = true;
+      int seg = 0;                      // segments (tile shares) started so far
+      for (int i = 0; i < n_iter && ok; ++i) {
+        const int it = sch.it0 + i;
+        const int a = it % C::ATOMS;
+        const bool seg_first = (i == 0) || (a == 0);
+        const bool seg_last = (a == C::ATOMS - 1) || (it == sch.it1 - 1);
+        const int b = seg & 1;
+        if (seg_first &&
+            !mbar_wait_bounded(&acce[b], ((seg >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        const int s = i % STAGES;
+        if (!mbar_wait_bounded(&conv[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t st = smem_base + s * C::STAGE;
+        const uint64_t bdesc = make_sdesc_sw128(st + C::OFF_B);
+#pragma unroll
+        for (int w = 0; w < C::NW; ++w) {
+          const uint64_t adesc = make_sdesc_sw128(st + C::OFF_W16 + w * C::W16_TILE);
+          const uint32_t d = tmem_base + (uint32_t)(b * C::ACC + w * BN);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)   // 4 x K=16 f16 per 128-byte atom; +32 B = +2 in addr>>4
+            tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (seg_first && k == 0) ? 0u : 1u);
+        }
+        tc_commit(&empty[s]);
+        if (seg_last) { tc_commit(&accf[b]); ++seg; }
+      }
+      if (!ok) raise_error(p.err, kDevTimeoutMma);
+      tc_commit(drain);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {}
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ weight converters
+    // Warp q converts rows 32q..32q+31 of each weight tile: 8 rows per step,
+    // 4 lanes per row, 16 e4m3 (one 16-byte load) per lane -> 32 bytes of f16.
+    const int q = warp - 2;
+    for (int i = 0; i < n_iter; ++i) {
+      const int it = sch.it0 + i;
+      const int u = it / C::ATOMS, a = it % C::ATOMS;
+      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      const int e = p.tiles[mt].x;
+      const int s = i % STAGES;
+      float wsc[C::NW];
+#pragma unroll
+      for (int w = 0; w < C::NW; ++w) {
+        const int nb = KIND == 1 ? nt + w * (kInter / 128) : nt;
+        wsc[w] = __ldg(p.w_scale + ((size_t)e * (C::W_ROWS / 128) + nb) * (C::K / 128) + a / 2);
+      }
+      if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) break;
+      const uint8_t* st = smem + s * C::STAGE;
+      const int part = lane & 3;
+#pragma unroll
+      for (int w = 0; w < C::NW; ++w) {
+        uint4 src[4];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int row = q * 32 + rr * 8 + (lane >> 2);
+          src[rr] = *reinterpret_cast<const uint4*>(st + w * C::W8_TILE + row * 64 + part * 16);
+        }
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int row = q * 32 + rr * 8 + (lane >> 2);
+          uint4 lo, hi;
+          e4m3x16_to_f16(src[rr], wsc[w], lo, hi);
+          uint8_t* dst = const_cast<uint8_t*>(st) + C::OFF_W16 + w * C::W16_TILE + row * 128;
+          *reinterpret_cast<uint4*>(dst + (((2 * part) ^ (row & 7)) * 16)) = lo;
+          *reinterpret_cast<uint4*>(dst + (((2 * part + 1) ^ (row & 7)) * 16)) = hi;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&conv[s]);
+    }
+    if (*abort_flag) raise_error(p.err, kDevTimeoutProducer);
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int et = threadIdx.x - 192;           // 0..127
+    const int qq = warp & 3;                    // TMEM lane quarter of this warp
+    const int f = qq * 32 + lane;               // weight row inside the tile
+    const uint32_t lane_addr = (uint32_t)(qq * 32) << 16;
+    int seg = 0;
+    int seg_a0 = 0;
+    for (int i = 0; i < n_iter; ++i) {
+      const int it = sch.it0 + i;
+      const int u = it / C::ATOMS, a = it % C::ATOMS;
+      if (i == 0 || a == 0) seg_a0 = a;
+      const bool seg_last = (a == C::ATOMS - 1) || (it == sch.it1 - 1);
+      if (!seg_last) continue;
+      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      const int4 tile = p.tiles[mt];
+      const int b = seg & 1;
+      const bool got = mbar_wait_bounded(&accf[b], (seg >> 1) & 1, abort_flag);
+      if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
+      tc_fence_after();
+      const uint32_t acc0 = tmem_base + lane_addr + (uint32_t)(b * C::ACC);
+      const bool full_tile = (seg_a0 == 0 && a == C::ATOMS - 1);
+      bool finish = true;
+      int c_lo = 0, c_hi = -1;
+      if (!full_tile) {
+        // publish this CTA's share: [slot][w][token][128 rows] fp32
+        const int first_unit = sch.it0 / C::ATOMS;
+        const int slot = (u == first_unit) ? 0 : 1;
+        float* mine = p.partials + ((size_t)(blockIdx.x * 2 + slot) * C::NW) * BN * 128;
+#pragma unroll 1
+        for (int w = 0; w < C::NW; ++w)
+#pragma unroll 1
+          for (int c0 = 0; c0 < BN; c0 += 16) {
+            float v[16];
+            tmem_ld16(acc0 + w * BN + c0, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int x = 0; x < 16; ++x) __stcg(mine + ((size_t)w * BN + c0 + x) * 128 + f, v[x]);
+          }
+        __threadfence();
+        c_lo = (u * C::ATOMS) / sch.L;
+        c_hi = ((u + 1) * C::ATOMS - 1) / sch.L;
+        named_bar_sync(1, 128);
+        if (et == 0) {
+          const int old = atomicAdd(p.counters + u, 1);
+          last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
+        }
+        named_bar_sync(1, 128);
+        finish = last_flag[0] != 0;
+        if (finish) __threadfence();
+      }
+      if (finish) {
+        // Column chunks of 16 tokens: full sums (TMEM, or published partials in
+        // fixed CTA order), then the epilogue of this GEMM.
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          float v[C::NW][16];
+          if (full_tile) {
+#pragma unroll
+            for (int w = 0; w < C::NW; ++w) tmem_ld16(acc0 + w * BN + c0, v[w]);
+            tmem_ld_wait();
+          } else {
+#pragma unroll
+            for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+              for (int x = 0; x < 16; ++x) v[w][x] = 0.f;
+            for (int c = c_lo; c <= c_hi; ++c) {
+              const int cslot = (u == (c * sch.L) / C::ATOMS) ? 0 : 1;
+              const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
+#pragma unroll
+              for (int w = 0; w < C::NW; ++w)
+#pragma unroll
+                for (int x = 0; x < 16; ++x) v[w][x] += __ldcg(src + ((size_t)w * BN + c0 + x) * 128 + f);
+            }
+          }
+#pragma unroll
+          for (int x = 0; x < 16; ++x) {
+            const int j = c0 + x;
+            if (j >= tile.z) break;
+            const size_t row = (size_t)(tile.y + j);
+            if (KIND == 1) {
+              const float x1 = v[0][x], x2 = v[C::NW - 1][x];
+              const float cv = x2 * __frcp_rn(1.0f + __expf(-x2)) * x1;
+              p.inter16[row * kInter + nt * 128 + f] = __float2half_rn(cv);
+            } else {
+              p.down[row * kHidden + nt * 128 + f] = v[0][x];
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acce[b]);
+      ++seg;
+    }
+    if (*abort_flag) raise_error(p.err, kDevTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------------------
+// Host-side dispatch
+// --------------------------------------------------------------------------
+template <int KIND, int BN> struct B16Pick;
+template <> struct B16Pick<1, 64> { static constexpr int S = 4; };
+template <> struct B16Pick<1, 128> { static constexpr int S = 3; };
+template <> struct B16Pick<2, 64> { static constexpr int S = 4; };
+template <> struct B16Pick<2, 128> { static constexpr int S = 4; };
+template <> struct B16Pick<2, 256> { static constexpr int S = 3; };
+
+#define MOE_B16_CASES(X) X(1, 64) X(1, 128) X(2, 64) X(2, 128) X(2, 256)
+
+template <int KIND, int BN>
+static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
+                                  int grid, cudaStream_t st) {
+  constexpr int S = B16Pick<KIND, BN>::S;
+  using C = B16Cfg<KIND, BN, S>;
+  auto kern = moe_gemm_f16_kernel<KIND, BN, S>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
+}
+
+size_t gemm_f16_partials_bytes(int kind, int bn, int grid) {
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return (size_t)grid * 2 * B16Cfg<KD, BB, 1>::NW * BB * 128 * sizeof(float);
+  MOE_B16_CASES(X)
+#undef X
+  return 0;
+}
+
+cudaError_t launch_gemm_f16(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
+                             const GemmParams& p, int grid, cudaStream_t st) {
+#define X(KD, BB) \
+  if (kind == KD && bn == BB) return launch_f16_one<KD, BB>(tm_w, tm_b, p, grid, st);
+  MOE_B16_CASES(X)
+#undef X
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace moe

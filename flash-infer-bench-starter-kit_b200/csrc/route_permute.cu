@@ -338,7 +338,8 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
                const int32_t* __restrict__ bases, int T, int E_l, int local_offset, int R_cap,
                const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
                int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
-               uint8_t* __restrict__ act, float* __restrict__ act_scale) {
+               uint8_t* __restrict__ act, float* __restrict__ act_scale,
+               __half* __restrict__ act16) {
   __shared__ int s_row[kPermBlock * kTopK];
   griddep_wait();
   griddep_launch_dependents();
@@ -359,7 +360,9 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
   }
   s_row[threadIdx.x] = row;
   __syncthreads();
-  // copy: 16-byte vectors, (pair, vector) flattened over the CTA
+  // copy: 16-byte vectors, (pair, vector) flattened over the CTA.  With act16
+  // the rows are written in f16 with their 1x128 scales applied (operand of
+  // the f16 GEMMs); otherwise as e4m3 plus the scales.
   constexpr int kVec = kGatherChunk / 16;
   const size_t col = (size_t)blockIdx.y * kGatherChunk;
   for (int v = threadIdx.x; v < kPermBlock * kTopK * kVec; v += blockDim.x) {
@@ -368,16 +371,27 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
     if (r < 0) continue;
     const int tok = blockIdx.x * kPermBlock + pr / kTopK;
     const int off = (v % kVec) * 16;
-    *reinterpret_cast<uint4*>(act + (size_t)r * kHidden + col + off) =
-        __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)tok * kHidden + col + off));
+    const uint4 val = __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)tok * kHidden + col + off));
+    if (act16) {
+      const int kb = (int)((col + off) / kBlock);
+      const float sc = __ldg(hs_scale + (size_t)kb * T + tok);
+      uint4 lo, hi;
+      e4m3x16_to_f16(val, sc, lo, hi);
+      uint4* dst = reinterpret_cast<uint4*>(act16 + (size_t)r * kHidden + col + off);
+      dst[0] = lo;
+      dst[1] = hi;
+    } else {
+      *reinterpret_cast<uint4*>(act + (size_t)r * kHidden + col + off) = val;
+    }
   }
-  const int r = s_row[threadIdx.x];
-  if (r >= 0) {
-    const int tok = t;
-    const int kb0 = blockIdx.y * (kGatherChunk / kBlock);
+  if (!act16) {
+    const int r = s_row[threadIdx.x];
+    if (r >= 0) {
+      const int kb0 = blockIdx.y * (kGatherChunk / kBlock);
 #pragma unroll
-    for (int q = 0; q < kGatherChunk / kBlock; ++q)
-      act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + tok);
+      for (int q = 0; q < kGatherChunk / kBlock; ++q)
+        act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + t);
+    }
   }
 }
 
@@ -630,12 +644,12 @@ cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB,
 cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
-                           uint8_t* act, float* act_scale, cudaStream_t st) {
+                           uint8_t* act, float* act_scale, __half* act16, cudaStream_t st) {
   const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
   return launch_pdl(scatter_kernel, dim3(nb, kGatherChunks), dim3(kPermBlock * kTopK), 0, st, ids,
                     masks8, NB8p, bases, T, E_l, local_offset, R_cap, static_cast<const uint8_t*>(hidden),
-                    hs_scale, inv_row, row_token, act, act_scale);
+                    hs_scale, inv_row, row_token, act, act_scale, act16);
 }
 
 cudaError_t launch_front(const float* logits, const void* bias, int T, float scaling, int local_offset,
