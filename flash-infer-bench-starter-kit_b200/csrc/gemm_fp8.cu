@@ -46,6 +46,10 @@
 
 namespace moe {
 
+#ifndef MOE_GEMM_PROBE_NOEPI
+#define MOE_GEMM_PROBE_NOEPI 0   // diagnostics builds only: skip the promotion arithmetic
+#endif
+
 #ifdef MOE_GEMM_TIMELINE
 // Diagnostics builds only: per-CTA %globaltimer stamps of pipeline milestones.
 __device__ unsigned long long g_timeline[2][1024][8];
@@ -291,7 +295,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (got) {
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < KS; ++kk) {
+        for (int kk = 0; kk < KS * (MOE_GEMM_PROBE_NOEPI == 0); ++kk) {
 #pragma unroll
           for (int w = 0; w < C::NW; ++w) {
             const float* coef = sl + (kk * C::NW + w) * BN + j0;
@@ -470,11 +474,11 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 template <int KIND, int BN> struct Pick;
 template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
-template <> struct Pick<1, 64> { static constexpr int S = 5, W = 2, K = 1, O = 1; };
+template <> struct Pick<1, 64> { static constexpr int S = 2, W = 2, K = 2, O = 1; };
 template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
 template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2, O = 1; };
 template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2, O = 1; };
-template <> struct Pick<2, 64> { static constexpr int S = 6, W = 1, K = 1, O = 1; };
+template <> struct Pick<2, 64> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
 
 template <int KIND, int BN>
