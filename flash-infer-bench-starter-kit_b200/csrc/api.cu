@@ -30,7 +30,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
 int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
-constexpr int kWideMinTokens = 4096;
+constexpr int kWideMinTokens = 6144;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -91,8 +91,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  // f16-operand GEMMs win once experts see ~128 tokens each (measured on B200:
-  // equal at T=4096, 25% faster at T=8192, slower below).
+  // f16-operand GEMMs win once experts see ~190+ tokens each (measured on
+  // B200 with 32 local experts: 10% slower at T=4096, 7% faster at T=8192).
   P->wide = g_path_override == 2 || (g_path_override == 0 && T >= kWideMinTokens);
   if (P->wide) {
     // f16 kernels accumulate in TMEM, so tiles are as wide as TMEM allows:

@@ -129,7 +129,8 @@ STAGE_CASES = [
     (130, 16, 16, 15, 0.0, (64, 32)),
     (300, 8, 0, 16, 0.0, (0, 0)),          # T > 256: 3-kernel front end, e4m3 GEMMs
     (300, 8, 0, 16, 0.0, (0, 0, 2)),       # f16-operand GEMMs forced at a small batch (64-token tiles)
-    (4200, 8, 0, 17, 0.0, (0, 0)),         # f16 GEMMs with 128- and 256-token tiles
+    (4200, 8, 0, 17, 0.0, (0, 0)),         # e4m3 GEMMs, 64/128-token tiles, many rows
+    (4200, 8, 0, 17, 0.0, (0, 0, 2)),      # f16 GEMMs with 128- and 256-token tiles
 ]
 
 
@@ -138,7 +139,7 @@ def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
     inp = cached_inputs(T, E_l, off, seed, skew)
     path = bn[2] if len(bn) > 2 else 0
     out, ws, lay = run_layer(pkg, to_dev(inp, cuda_dev), bn=bn[:2], path=path)
-    wide = path == 2 or (path == 0 and T >= 4096)
+    wide = path == 2 or (path == 0 and T >= 6144)
     R = lay.row_capacity
     # routing
     ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
