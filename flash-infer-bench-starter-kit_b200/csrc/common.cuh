@@ -86,6 +86,20 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 }
 // Order this thread's earlier (generic-proxy) observations before its later
 // async-proxy (TMA) accesses.
+// Work unit u of a grouped GEMM -> (token tile mt, weight tile nt), token-tile
+// major: the CTAs running at the same time cover a few token tiles with all of
+// their weight tiles, so the two or three token tiles of one expert read each
+// weight tile from L2 rather than from HBM again, and each expert's tiles finish
+// together (the early-start consumer waits per expert).
+__device__ __forceinline__ int2 unit_tile(int u, int n_mt, int NT) {
+#ifdef MOE_UNIT_NT_MAJOR
+  return make_int2(u % n_mt, u / n_mt);
+#else
+  (void)n_mt;
+  return make_int2(u / NT, u % NT);
+#endif
+}
+
 __device__ __forceinline__ void fence_proxy_async() {
   asm volatile("fence.proxy.async;" ::: "memory");
 }

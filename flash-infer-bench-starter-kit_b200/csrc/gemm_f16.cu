@@ -30,6 +30,12 @@
 
 namespace moe {
 
+// Diagnostics builds only: drop the weight conversion (1) or the MMAs (2) to
+// see which stage bounds the pipeline.
+#ifndef MOE_F16_PROBE
+#define MOE_F16_PROBE 0
+#endif
+
 template <int KIND, int BN, int STAGES>
 struct B16Cfg {
   static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles (X1, X2) per stage
@@ -72,10 +78,6 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-struct B16Schedule {
-  int n_mt, units, total, L, it0, it1;
-};
-
 template <int KIND, int BN, int STAGES>
 __global__ void __launch_bounds__(320, 1)
 moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
@@ -99,15 +101,9 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
 
   griddep_wait();
   griddep_launch_dependents();
-  B16Schedule sch;
-  sch.n_mt = p.sched[KIND - 1];
-  sch.units = sch.n_mt * C::NT;
-  sch.total = sch.units * C::ATOMS;
-  sch.L = (sch.total + gridDim.x - 1) / gridDim.x;
-  sch.it0 = min(sch.total, (int)blockIdx.x * sch.L);
-  sch.it1 = min(sch.total, sch.it0 + sch.L);
-  if (sch.it0 >= sch.it1) return;
-  const int n_iter = sch.it1 - sch.it0;
+  const WorkSched sch = make_work_sched(p.sched[KIND - 1], C::NT, C::ATOMS);
+  const int n_iter = sch.n_iter();
+  if (n_iter == 0) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -135,9 +131,10 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       int issued = 0;
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
-        const int it = sch.it0 + i;
-        const int u = it / C::ATOMS, a = it % C::ATOMS;
-        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+        int u, a, r;
+        sch.at(i, C::ATOMS, u, a, r);
+        const int2 mn = unit_tile(u, sch.n_mt, C::NT);
+        const int mt = mn.x, nt = mn.y;
         const int4 tile = p.tiles[mt];
         const int s = i % STAGES;
         if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -163,16 +160,20 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_lane()) {
-      constexpr uint32_t idesc = make_idesc_f16(128, BN);
       const uint32_t smem_base = smem_u32(smem);
+      uint32_t idesc = 0;
       bool ok = true;
       int seg = 0;                      // segments (tile shares) started so far
       for (int i = 0; i < n_iter && ok; ++i) {
-        const int it = sch.it0 + i;
-        const int a = it % C::ATOMS;
-        const bool seg_first = (i == 0) || (a == 0);
-        const bool seg_last = (a == C::ATOMS - 1) || (it == sch.it1 - 1);
+        int u, a, r;
+        sch.at(i, C::ATOMS, u, a, r);
+        const bool seg_first = (i == sch.n1) || (a == 0);
+        const bool seg_last = (a == C::ATOMS - 1) || (i == n_iter - 1);
         const int b = seg & 1;
+        if (seg_first) {   // MMA N covers the tile's rows only
+          const int rows = p.tiles[unit_tile(u, sch.n_mt, C::NT).x].z;
+          idesc = make_idesc_f16(128, min(BN, (rows + 15) & ~15));
+        }
         if (seg_first &&
             !mbar_wait_bounded(&acce[b], ((seg >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
         const int s = i % STAGES;
@@ -185,7 +186,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
           const uint64_t adesc = make_sdesc_sw128(st + C::OFF_W16 + w * C::W16_TILE);
           const uint32_t d = tmem_base + (uint32_t)(b * C::ACC + w * BN);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)   // 4 x K=16 f16 per 128-byte atom; +32 B = +2 in addr>>4
+          for (int k = 0; k < 4 * (MOE_F16_PROBE != 2); ++k)   // 4 x K=16 per 128-byte atom; +32 B = +2 in addr>>4
             tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (seg_first && k == 0) ? 0u : 1u);
         }
         tc_commit(&empty[s]);
@@ -202,9 +203,10 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
     // 4 lanes per row, 16 e4m3 (one 16-byte load) per lane -> 32 bytes of f16.
     const int q = warp - 2;
     for (int i = 0; i < n_iter; ++i) {
-      const int it = sch.it0 + i;
-      const int u = it / C::ATOMS, a = it % C::ATOMS;
-      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      int u, a, r;
+      sch.at(i, C::ATOMS, u, a, r);
+      const int2 mn = unit_tile(u, sch.n_mt, C::NT);
+        const int mt = mn.x, nt = mn.y;
       const int e = p.tiles[mt].x;
       const int s = i % STAGES;
       float wsc[C::NW];
@@ -217,7 +219,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       const uint8_t* st = smem + s * C::STAGE;
       const int part = lane & 3;
 #pragma unroll
-      for (int w = 0; w < C::NW; ++w) {
+      for (int w = 0; w < C::NW * (MOE_F16_PROBE != 1); ++w) {
         uint4 src[4];
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
@@ -248,12 +250,13 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
     int seg = 0;
     int seg_a0 = 0;
     for (int i = 0; i < n_iter; ++i) {
-      const int it = sch.it0 + i;
-      const int u = it / C::ATOMS, a = it % C::ATOMS;
-      if (i == 0 || a == 0) seg_a0 = a;
-      const bool seg_last = (a == C::ATOMS - 1) || (it == sch.it1 - 1);
+      int u, a, r;
+      sch.at(i, C::ATOMS, u, a, r);
+      if (i == sch.n1 || a == 0) seg_a0 = a;
+      const bool seg_last = (a == C::ATOMS - 1) || (i == n_iter - 1);
       if (!seg_last) continue;
-      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      const int2 mn = unit_tile(u, sch.n_mt, C::NT);
+      const int mt = mn.x, nt = mn.y;
       const int4 tile = p.tiles[mt];
       const int b = seg & 1;
       const bool got = mbar_wait_bounded(&accf[b], (seg >> 1) & 1, abort_flag);
@@ -265,13 +268,12 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       int c_lo = 0, c_hi = -1;
       if (!full_tile) {
         // publish this CTA's share: [slot][w][token][128 rows] fp32
-        const int first_unit = sch.it0 / C::ATOMS;
-        const int slot = (u == first_unit) ? 0 : 1;
+        const int slot = sch.slot(blockIdx.x, r, C::ATOMS);
         float* mine = p.partials + ((size_t)(blockIdx.x * 2 + slot) * C::NW) * BN * 128;
 #pragma unroll 1
         for (int w = 0; w < C::NW; ++w)
 #pragma unroll 1
-          for (int c0 = 0; c0 < BN; c0 += 16) {
+          for (int c0 = 0; c0 < tile.z; c0 += 16) {
             float v[16];
             tmem_ld16(acc0 + w * BN + c0, v);
             tmem_ld_wait();
@@ -279,8 +281,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
             for (int x = 0; x < 16; ++x) __stcg(mine + ((size_t)w * BN + c0 + x) * 128 + f, v[x]);
           }
         __threadfence();
-        c_lo = (u * C::ATOMS) / sch.L;
-        c_hi = ((u + 1) * C::ATOMS - 1) / sch.L;
+        c_lo = sch.first_cta(r, C::ATOMS);
+        c_hi = sch.last_cta(r, C::ATOMS);
         named_bar_sync(1, 128);
         if (et == 0) {
           const int old = atomicAdd(p.counters + u, 1);
@@ -294,7 +296,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         // Column chunks of 16 tokens: full sums (TMEM, or published partials in
         // fixed CTA order), then the epilogue of this GEMM.
 #pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 16) {
+        for (int c0 = 0; c0 < tile.z; c0 += 16) {
           float v[C::NW][16];
           if (full_tile) {
 #pragma unroll
@@ -306,7 +308,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
 #pragma unroll
               for (int x = 0; x < 16; ++x) v[w][x] = 0.f;
             for (int c = c_lo; c <= c_hi; ++c) {
-              const int cslot = (u == (c * sch.L) / C::ATOMS) ? 0 : 1;
+              const int cslot = sch.slot(c, r, C::ATOMS);
               const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
 #pragma unroll
               for (int w = 0; w < C::NW; ++w)

@@ -90,21 +90,6 @@ struct GemmCfg {
   static_assert(TMEM_COLS * OCC <= 512, "TMEM budget per SM");
 };
 
-struct Schedule {
-  int n_mt, units, total, L, it0, it1;
-};
-
-__device__ __forceinline__ Schedule make_schedule(int n_mt, int NT, int KSTEPS) {
-  Schedule s;
-  s.n_mt = n_mt;
-  s.units = n_mt * NT;
-  s.total = s.units * KSTEPS;
-  s.L = (s.total + gridDim.x - 1) / gridDim.x;
-  s.it0 = min(s.total, (int)blockIdx.x * s.L);
-  s.it1 = min(s.total, s.it0 + s.L);
-  return s;
-}
-
 template <int KIND, int BN, int STAGES, int NWG, int KS, int OCC>
 __global__ void __launch_bounds__(GemmCfg<KIND, BN, STAGES, NWG, KS, OCC>::THREADS, OCC)
 moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
@@ -135,9 +120,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   if (KIND == 1 || !p.early_start) griddep_wait();
   if (threadIdx.x == 0) MOE_TL(1);
   griddep_launch_dependents();
-  const Schedule sch = make_schedule(p.sched[KIND - 1], C::NT, C::KSTEPS);
-  if (sch.it0 >= sch.it1) return;   // uniform: this CTA has no work
-  const int n_iter = sch.it1 - sch.it0;
+  const WorkSched sch = make_work_sched(p.sched[KIND - 1], C::NT, C::KSTEPS);
+  const int n_iter = sch.n_iter();
+  if (n_iter == 0) return;   // uniform: this CTA has no work
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -162,9 +147,10 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       int ready_e = -1;                 // GEMM2: expert whose intermediate is known complete
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
-        const int it = sch.it0 + i;
-        const int u = it / C::KSTEPS, ks = it % C::KSTEPS;
-        const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+        int u, ks, r;
+        sch.at(i, C::KSTEPS, u, ks, r);
+        const int2 mn = unit_tile(u, sch.n_mt, C::NT);
+        const int mt = mn.x, nt = mn.y;
         const int4 tile = p.tiles[mt];
         const int s = i % STAGES;
         if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -198,11 +184,19 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (elect_one_lane()) {
-      constexpr uint32_t idesc = make_idesc_f8(128, C::MMA_N);
       const uint32_t smem_base = smem_u32(smem);
       bool ok = true;
+      int cur_u = -1;
+      uint32_t idesc = 0;
       for (int i = 0; i < n_iter; ++i) {
         const int s = i % STAGES, b = i % C::NBUF;
+        const int u = sch.unit_of(i, C::KSTEPS);
+        if (u != cur_u) {
+          // MMA N covers the tile's rows only (KIND 2: hi and lo row per token).
+          cur_u = u;
+          const int rows = (KIND == 1 ? 1 : 2) * p.tiles[unit_tile(u, sch.n_mt, C::NT).x].z;
+          idesc = make_idesc_f8(128, min(C::MMA_N, (rows + 15) & ~15));
+        }
         if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
         if (i == 0) MOE_TL(2);
         if (!mbar_wait_bounded(&tempty[b], ((i / C::NBUF) & 1) ^ 1, abort_flag)) { ok = false; break; }
@@ -252,14 +246,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     const int my_kk = et / (C::NW * BN), my_w = (et / BN) % C::NW, my_j = et % BN;
     int pf_unit = -1, pf_col = -1, pf_e = 0, pf_nt = 0;
     auto fetch = [&](int i_t) -> float {
-      const int it_t = sch.it0 + i_t;
-      const int u_t = it_t / C::KSTEPS;
-      const int kb_t = (it_t % C::KSTEPS) * KS + my_kk;
+      int u_t, ks_t, r_t;
+      sch.at(i_t, C::KSTEPS, u_t, ks_t, r_t);
+      const int kb_t = ks_t * KS + my_kk;
       if (u_t != pf_unit) {
         pf_unit = u_t;
-        const int4 tl = p.tiles[u_t % sch.n_mt];
+        const int2 mn = unit_tile(u_t, sch.n_mt, C::NT);
+        const int4 tl = p.tiles[mn.x];
         pf_e = tl.x;
-        pf_nt = u_t / sch.n_mt;
+        pf_nt = mn.y;
         pf_col = my_j < tl.z ? tl.y + my_j : -1;
         if (KIND == 2 && p.early_start && pf_col >= 0) {   // the intermediate's scales come from GEMM1
           const int cnt = p.seg[pf_e + 1] - p.seg[pf_e];
@@ -277,11 +272,12 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     named_bar_sync(1, C::NEPI);
 
     for (int i = 0; i < n_iter; ++i) {
-      const int it = sch.it0 + i;
-      const int u = it / C::KSTEPS, ks = it % C::KSTEPS;
-      const int nt = u / sch.n_mt, mt = u % sch.n_mt;
+      int u, ks, r;
+      sch.at(i, C::KSTEPS, u, ks, r);
+      const int2 mn = unit_tile(u, sch.n_mt, C::NT);
+      const int mt = mn.x, nt = mn.y;
       const int b = i % C::NBUF;
-      if (i == 0 || ks == 0) {
+      if (i == sch.n1 || ks == 0) {
         tile = p.tiles[mt];
         seg_k0 = ks;
 #pragma unroll
@@ -308,6 +304,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             const uint32_t tcol = col0 + (KIND == 1 ? j0 : 2 * j0);
 #pragma unroll
             for (int c = 0; c < NLD; c += 2) {
+              // Columns past the tile's rows hold no MMA result: skip them.
+              if (j0 + c * (KIND == 1 ? LDC : LDC / 2) >= tile.z) break;
               float v[2][LDC];
               tmem_ld<LDC>(tmem_base + lane_addr + tcol + c * LDC, v[0]);
               if (c + 1 < NLD) tmem_ld<LDC>(tmem_base + lane_addr + tcol + (c + 1) * LDC, v[1]);
@@ -345,15 +343,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (loader && i + 2 < n_iter) sring[((i + 2) % C::RING) * C::SLOT + et] = pre;
       if (named_bar_or(1, C::NEPI, *abort_flag != 0)) break;   // uniform abort decision
 
-      const bool seg_last = (ks == C::KSTEPS - 1) || (it == sch.it1 - 1);
+      const bool seg_last = (ks == C::KSTEPS - 1) || (i == n_iter - 1);
       if (et == 0 && i == n_iter - 1) MOE_TL(6);
       if (!seg_last) continue;
 
       // ---------------- end of this CTA's share of unit u
       if (!(seg_k0 == 0 && ks == C::KSTEPS - 1)) {
         // stream-K: publish the partial, the last contributor finishes the unit
-        const int first_unit = sch.it0 / C::KSTEPS;
-        const int slot = (u == first_unit) ? 0 : 1;
+        const int slot = sch.slot(blockIdx.x, r, C::KSTEPS);
         float* mine = p.partials + ((size_t)(blockIdx.x * 2 + slot) * C::NW) * BN * 128;
 #pragma unroll
         for (int w = 0; w < C::NW; ++w)
@@ -362,8 +359,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             __stcg(mine + ((size_t)w * BN + j0 + jj) * 128 + f, acc[w][jj]);
         __threadfence();
         named_bar_sync(1, C::NEPI);
-        const int c_lo = (u * C::KSTEPS) / sch.L;
-        const int c_hi = ((u + 1) * C::KSTEPS - 1) / sch.L;
+        const int c_lo = sch.first_cta(r, C::KSTEPS);
+        const int c_hi = sch.last_cta(r, C::KSTEPS);
         if (et == 0) {
           const int old = atomicAdd(p.counters + u, 1);
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
@@ -376,7 +373,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           // Two contributors: fp32 addition is commutative, so adding the other
           // CTA's partial to our registers is the same sum whoever is last.
           const int c = (c_lo == (int)blockIdx.x) ? c_hi : c_lo;
-          const int cslot = (u == (c * sch.L) / C::KSTEPS) ? 0 : 1;
+          const int cslot = sch.slot(c, r, C::KSTEPS);
           const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
           float other[C::NW][C::CPW];
 #pragma unroll
@@ -395,7 +392,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
             for (int jj = 0; jj < C::CPW; ++jj) acc[w][jj] = 0.f;
           for (int c = c_lo; c <= c_hi; ++c) {
-            const int cslot = (u == (c * sch.L) / C::KSTEPS) ? 0 : 1;
+            const int cslot = sch.slot(c, r, C::KSTEPS);
             const float* src = p.partials + ((size_t)(c * 2 + cslot) * C::NW) * BN * 128;
 #pragma unroll
             for (int w = 0; w < C::NW; ++w)

@@ -25,6 +25,60 @@ struct GemmParams {
   int R_cap;
 };
 
+// Persistent schedule of a grouped GEMM: units (token tile x weight tile, see
+// unit_tile) of ITERS pipeline iterations each, over gridDim.x CTAs.
+//   phase 1: floor(units / G) full waves; in wave w CTA c runs unit w*G + c,
+//            so the CTAs running at one time cover G consecutive units, which
+//            share token tiles and weight tiles in L2;
+//   phase 2: the R < G remaining units, as one contiguous stream-K range of
+//            ceil(R*ITERS / G) iterations per CTA.  A unit split between CTAs
+//            is finished by its last contributor (fixed-order reduction).
+struct WorkSched {
+  int n_mt, units, Wf, n1, it0, it1, L;
+  __device__ __forceinline__ int n_iter() const { return n1 + it1 - it0; }
+  // Local iteration i -> unit u, iteration a inside the unit, and the unit's
+  // phase-2 index r (-1 in phase 1: never split).
+  __device__ __forceinline__ void at(int i, int ITERS, int& u, int& a, int& r) const {
+    if (i < n1) {
+      u = (i / ITERS) * (int)gridDim.x + (int)blockIdx.x;
+      a = i % ITERS;
+      r = -1;
+    } else {
+      const int it = it0 + i - n1;
+      r = it / ITERS;
+      a = it % ITERS;
+      u = Wf * (int)gridDim.x + r;
+    }
+  }
+  __device__ __forceinline__ int unit_of(int i, int ITERS) const {
+    int u, a, r;
+    at(i, ITERS, u, a, r);
+    return u;
+  }
+  // First CTA and last CTA contributing to phase-2 unit r.
+  __device__ __forceinline__ int first_cta(int r, int ITERS) const { return (r * ITERS) / L; }
+  __device__ __forceinline__ int last_cta(int r, int ITERS) const { return ((r + 1) * ITERS - 1) / L; }
+  // Partial-tile slot CTA c uses for phase-2 unit r: 0 for the unit its range
+  // starts in, 1 for the one it ends in.
+  __device__ __forceinline__ int slot(int c, int r, int ITERS) const {
+    return r == (c * L) / ITERS ? 0 : 1;
+  }
+};
+
+__device__ __forceinline__ WorkSched make_work_sched(int n_mt, int NT, int ITERS) {
+  WorkSched s;
+  const int G = gridDim.x;
+  s.n_mt = n_mt;
+  s.units = n_mt * NT;
+  s.Wf = s.units / G;
+  s.n1 = s.Wf * ITERS;
+  const int total2 = (s.units - s.Wf * G) * ITERS;
+  s.L = max(1, (total2 + G - 1) / G);
+  s.it0 = min(total2, (int)blockIdx.x * s.L);
+  s.it1 = min(total2, s.it0 + s.L);
+  return s;
+}
+
 // Token-tile configurations compiled for each GEMM (BN = tokens per tile).
 constexpr int kNumBnConfigs = 4;
 constexpr int kBnConfigs[kNumBnConfigs] = {16, 32, 64, 128};

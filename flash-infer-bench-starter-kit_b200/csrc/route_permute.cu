@@ -216,6 +216,15 @@ __device__ __forceinline__ uint32_t block_mask(const uint8_t* __restrict__ masks
 // Scan: per-expert row segments, per-(CTA, expert) row bases, GEMM tile
 // lists, and zeroed stream-K counters.  One CTA of 1024 threads.
 // --------------------------------------------------------------------------
+// Token tile m of the n = ceil(cnt / bn) tiles of one expert's cnt rows.  The
+// rows are split evenly (tile sizes differ by at most one) rather than as
+// full tiles plus a remainder, so no tile is nearly empty: the GEMMs size the
+// MMA's N to the tile, and an even split keeps that N small.
+__device__ __forceinline__ int4 balanced_tile(int e, int r0, int cnt, int n, int m) {
+  const int a = m * cnt / n, b = (m + 1) * cnt / n;
+  return make_int4(e, r0 + a, b - a, 0);
+}
+
 __device__ __forceinline__ int warp_exclusive_scan(int v, int lane, int* total) {
   int incl = v;
 #pragma unroll
@@ -307,9 +316,9 @@ scan_kernel(const uint8_t* __restrict__ masks8, int NB8p, int32_t* __restrict__ 
     const int cnt = s_cnt[e], r0 = s_seg[e];
     const int n1 = (cnt + bn1 - 1) / bn1, n2 = (cnt + bn2 - 1) / bn2;
     for (int m = lane; m < n1; m += 32)
-      tiles1[s_t1[e] + m] = make_int4(e, r0 + m * bn1, min(bn1, cnt - m * bn1), 0);
+      tiles1[s_t1[e] + m] = balanced_tile(e, r0, cnt, n1, m);
     for (int m = lane; m < n2; m += 32)
-      tiles2[s_t2[e] + m] = make_int4(e, r0 + m * bn2, min(bn2, cnt - m * bn2), 0);
+      tiles2[s_t2[e] + m] = balanced_tile(e, r0, cnt, n2, m);
   }
   const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
   for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
@@ -513,9 +522,9 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
       const int cnt = s_seg[e + 1] - s_seg[e], r0 = s_seg[e];
       const int n1 = (cnt + bn1 - 1) / bn1, n2 = (cnt + bn2 - 1) / bn2;
       for (int m = lane; m < n1; m += 32)
-        tiles1[s_t1[e] + m] = make_int4(e, r0 + m * bn1, min(bn1, cnt - m * bn1), 0);
+        tiles1[s_t1[e] + m] = balanced_tile(e, r0, cnt, n1, m);
       for (int m = lane; m < n2; m += 32)
-        tiles2[s_t2[e] + m] = make_int4(e, r0 + m * bn2, min(bn2, cnt - m * bn2), 0);
+        tiles2[s_t2[e] + m] = balanced_tile(e, r0, cnt, n2, m);
     }
     const int units1 = s_tot[1] * nt1, units2 = s_tot[2] * nt2;
     for (int i = threadIdx.x; i < units1; i += blockDim.x) counters1[i] = 0;
