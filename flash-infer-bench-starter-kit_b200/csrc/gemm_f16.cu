@@ -24,8 +24,8 @@
 // partial sums are published to global memory and added, in fixed CTA order,
 // by the last contributor.
 //
-// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2-5 weight
-// converters, 6-9 epilogue.
+// Warp roles: 0 TMA producer, 1 TMEM owner + MMA issuer, 2..2+NCONV-1 weight
+// converters, the last four the epilogue.
 #include "kernels.cuh"
 
 namespace moe {
@@ -35,8 +35,41 @@ namespace moe {
 #ifndef MOE_F16_PROBE
 #define MOE_F16_PROBE 0
 #endif
+#ifndef MOE_F16_NCONV
+#define MOE_F16_NCONV 8
+#endif
 
-template <int KIND, int BN, int STAGES>
+// Shared memory holds two rings:
+//   raw ring (RS stages): what TMA writes -- the e4m3 weight tile(s) and the
+//     f16 token tile; a stage is free once the MMA that read its tokens is done;
+//   operand ring (OS stages): the converted f16 weight tile(s) the MMA reads.
+// Only the raw ring waits on memory latency, so it gets most of the space:
+// deeper prefetch for the same shared memory than one ring of whole stages.
+// Weight conversion: e4m3 -> f16 by cvt (exact), then one f16 multiply by
+// f16(s * 2^8), s the 128x128 block scale.  The 2^8 keeps small products out
+// of the f16 subnormal range; the epilogue multiplies the fp32 accumulator by
+// 2^-8 (exact).  Dequantised weights must stay below 2^8 in magnitude.  The
+// scale's rounding to f16 adds at most 2^-11 relative to each weight block.
+constexpr float kAccUnscale = 1.0f / 256.0f;
+
+__device__ __forceinline__ void convert16(uint4 src, float scale, uint4& lo, uint4& hi) {
+  const uint32_t w[4] = {src.x, src.y, src.z, src.w};
+  const __half2 s2 = __float2half2_rn(scale * 256.0f);
+  uint32_t out[8];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * h)) & 0xFFFF);
+      __half2 v = __hmul2(__half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3)), s2);
+      out[i * 2 + h] = *reinterpret_cast<uint32_t*>(&v);
+    }
+  }
+  lo = make_uint4(out[0], out[1], out[2], out[3]);
+  hi = make_uint4(out[4], out[5], out[6], out[7]);
+}
+
+template <int KIND, int BN, int RS, int OS>
 struct B16Cfg {
   static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles (X1, X2) per stage
   static constexpr int K = KIND == 1 ? kHidden : kInter;    // reduction length
@@ -46,14 +79,19 @@ struct B16Cfg {
   static constexpr int W8_TILE = 128 * 64;                  // e4m3 staging: 128 rows x 64 B
   static constexpr int W16_TILE = 128 * 128;                // f16: 128 rows x 128 B (swizzled)
   static constexpr int B_TILE = BN * 128;                   // f16 tokens: BN rows x 128 B
-  static constexpr int OFF_W16 = NW * W8_TILE;
-  static constexpr int OFF_B = OFF_W16 + NW * W16_TILE;
-  static constexpr int STAGE = OFF_B + B_TILE;
+  static constexpr int OFF_B = NW * W8_TILE;               // token tile inside a raw stage
+  static constexpr int RAW = OFF_B + B_TILE;                // raw stage bytes
+  static constexpr int OPS = NW * W16_TILE;                 // operand stage bytes
+  static constexpr int OFF_OP = RS * RAW;                   // operand ring after the raw ring
   static constexpr int ACC = NW * BN;                       // TMEM columns of one tile accumulator
   static constexpr int TMEM_COLS = 2 * ACC <= 128 ? 128 : 2 * ACC <= 256 ? 256 : 512;
-  static constexpr int THREADS = 320;
-  static constexpr int SMEM = 1024 + STAGES * STAGE + 1024;
-  static_assert(STAGE % 1024 == 0, "1024-byte aligned stages");
+  static constexpr int NCONV = MOE_F16_NCONV;               // converter warps
+  static constexpr int EPI0 = 64 + 32 * NCONV;              // first epilogue thread
+  static constexpr int THREADS = EPI0 + 128;
+  static constexpr int CROWS = 128 / NCONV;                 // weight rows per converter warp
+  static_assert(CROWS % 8 == 0, "converter rows");
+  static constexpr int SMEM = 1024 + RS * RAW + OS * OPS + 1024;
+  static_assert(RAW % 1024 == 0 && OPS % 1024 == 0, "1024-byte aligned stages");
   static_assert(2 * ACC <= 512, "two TMEM accumulators");
   static_assert(BN % 16 == 0 && BN <= 256, "MMA N");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -78,18 +116,19 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int KIND, int BN, int STAGES>
-__global__ void __launch_bounds__(320, 1)
+template <int KIND, int BN, int RS, int OS>
+__global__ void __launch_bounds__(B16Cfg<KIND, BN, RS, OS>::THREADS, 1)
 moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
                      const GemmParams p) {
-  using C = B16Cfg<KIND, BN, STAGES>;
+  using C = B16Cfg<KIND, BN, RS, OS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* aux = smem + STAGES * C::STAGE;
-  uint64_t* full = reinterpret_cast<uint64_t*>(aux);       // TMA bytes of stage s landed
-  uint64_t* conv = full + STAGES;                           // converters wrote stage s
-  uint64_t* empty = conv + STAGES;                          // MMA finished with stage s
-  uint64_t* accf = empty + STAGES;                          // accumulator b complete
+  uint8_t* aux = smem + C::OFF_OP + OS * C::OPS;
+  uint64_t* full = reinterpret_cast<uint64_t*>(aux);       // TMA bytes of raw stage s landed
+  uint64_t* empty = full + RS;                              // MMA finished with raw stage s
+  uint64_t* conv = empty + RS;                              // converters wrote operand stage o
+  uint64_t* opempty = conv + OS;                            // MMA finished with operand stage o
+  uint64_t* accf = opempty + OS;                            // accumulator b complete
   uint64_t* acce = accf + 2;                                // accumulator b drained
   uint64_t* drain = acce + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -106,11 +145,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
   if (n_iter == 0) return;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 4);
-      mbar_init(&empty[s], 1);
-    }
+    for (int s = 0; s < RS; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int o = 0; o < OS; ++o) { mbar_init(&conv[o], C::NCONV); mbar_init(&opempty[o], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
     mbar_init(drain, 1);
     *const_cast<int*>(abort_flag) = 0;
@@ -134,12 +170,12 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         int u, a, r;
         sch.at(i, C::ATOMS, u, a, r);
         const int2 mn = unit_tile(u, sch.n_mt, C::NT);
-        const int mt = mn.x, nt = mn.y;
+      const int mt = mn.x, nt = mn.y;
         const int4 tile = p.tiles[mt];
-        const int s = i % STAGES;
-        if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], C::NW * C::W8_TILE + C::B_TILE);
-        uint8_t* st = smem + s * C::STAGE;
+        const int s = i % RS;
+        if (!mbar_wait_bounded(&empty[s], ((i / RS) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&full[s], C::RAW);
+        uint8_t* st = smem + s * C::RAW;
         // weights: e4m3 [rows][64 B] per tile (X1 then X2 for GEMM1)
         tma_load_3d(&tm_w, &full[s], st, 0, a, tile.x * C::W_ROWS + nt * 128, pol_w);
         if (KIND == 1)
@@ -150,9 +186,9 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       }
       if (!ok) {
         raise_error(p.err, kDevTimeoutProducer);
-        for (int i = max(0, issued - STAGES); i < issued; ++i) {
+        for (int i = max(0, issued - RS); i < issued; ++i) {
           const unsigned long long t0 = globaltimer_ns();
-          while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+          while (!mbar_try_wait(&full[i % RS], (i / RS) & 1) &&
                  globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
         }
       }
@@ -176,20 +212,23 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         }
         if (seg_first &&
             !mbar_wait_bounded(&acce[b], ((seg >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        const int s = i % STAGES;
-        if (!mbar_wait_bounded(&conv[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
+        // The converters waited for raw stage s before writing operand stage o,
+        // so conv[o] also orders the token tile's TMA writes before the MMA.
+        const int s = i % RS, o = i % OS;
+        if (!mbar_wait_bounded(&conv[o], (i / OS) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t st = smem_base + s * C::STAGE;
-        const uint64_t bdesc = make_sdesc_sw128(st + C::OFF_B);
+        const uint64_t bdesc = make_sdesc_sw128(smem_base + s * C::RAW + C::OFF_B);
+        const uint32_t op = smem_base + C::OFF_OP + o * C::OPS;
 #pragma unroll
         for (int w = 0; w < C::NW; ++w) {
-          const uint64_t adesc = make_sdesc_sw128(st + C::OFF_W16 + w * C::W16_TILE);
+          const uint64_t adesc = make_sdesc_sw128(op + w * C::W16_TILE);
           const uint32_t d = tmem_base + (uint32_t)(b * C::ACC + w * BN);
 #pragma unroll
           for (int k = 0; k < 4 * (MOE_F16_PROBE != 2); ++k)   // 4 x K=16 per 128-byte atom; +32 B = +2 in addr>>4
             tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (seg_first && k == 0) ? 0u : 1u);
         }
         tc_commit(&empty[s]);
+        tc_commit(&opempty[o]);
         if (seg_last) { tc_commit(&accf[b]); ++seg; }
       }
       if (!ok) raise_error(p.err, kDevTimeoutMma);
@@ -197,53 +236,55 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       const unsigned long long t0 = globaltimer_ns();
       while (!mbar_try_wait(drain, 0) && globaltimer_ns() - t0 < kWaitLimitNs) {}
     }
-  } else if (warp < 6) {
+  } else if (warp < 2 + C::NCONV) {
     // ------------------------------------------------------------ weight converters
-    // Warp q converts rows 32q..32q+31 of each weight tile: 8 rows per step,
+    // Warp q converts rows CROWS*q.. of each weight tile: 8 rows per step,
     // 4 lanes per row, 16 e4m3 (one 16-byte load) per lane -> 32 bytes of f16.
     const int q = warp - 2;
     for (int i = 0; i < n_iter; ++i) {
       int u, a, r;
       sch.at(i, C::ATOMS, u, a, r);
       const int2 mn = unit_tile(u, sch.n_mt, C::NT);
-        const int mt = mn.x, nt = mn.y;
+      const int mt = mn.x, nt = mn.y;
       const int e = p.tiles[mt].x;
-      const int s = i % STAGES;
+      const int s = i % RS, o = i % OS;
       float wsc[C::NW];
 #pragma unroll
       for (int w = 0; w < C::NW; ++w) {
         const int nb = KIND == 1 ? nt + w * (kInter / 128) : nt;
         wsc[w] = __ldg(p.w_scale + ((size_t)e * (C::W_ROWS / 128) + nb) * (C::K / 128) + a / 2);
       }
-      if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) break;
-      const uint8_t* st = smem + s * C::STAGE;
+      if (!mbar_wait_bounded(&full[s], (i / RS) & 1, abort_flag)) break;
+      if (!mbar_wait_bounded(&opempty[o], ((i / OS) & 1) ^ 1, abort_flag)) break;
+      const uint8_t* st = smem + s * C::RAW;
+      uint8_t* opst = smem + C::OFF_OP + o * C::OPS;
       const int part = lane & 3;
 #pragma unroll
       for (int w = 0; w < C::NW * (MOE_F16_PROBE != 1); ++w) {
-        uint4 src[4];
+        uint4 src[C::CROWS / 8];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const int row = q * 32 + rr * 8 + (lane >> 2);
+        for (int rr = 0; rr < C::CROWS / 8; ++rr) {
+          const int row = q * C::CROWS + rr * 8 + (lane >> 2);
           src[rr] = *reinterpret_cast<const uint4*>(st + w * C::W8_TILE + row * 64 + part * 16);
         }
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const int row = q * 32 + rr * 8 + (lane >> 2);
+        for (int rr = 0; rr < C::CROWS / 8; ++rr) {
+          const int row = q * C::CROWS + rr * 8 + (lane >> 2);
           uint4 lo, hi;
-          e4m3x16_to_f16(src[rr], wsc[w], lo, hi);
-          uint8_t* dst = const_cast<uint8_t*>(st) + C::OFF_W16 + w * C::W16_TILE + row * 128;
+          convert16(src[rr], wsc[w], lo, hi);
+          uint8_t* dst = opst + w * C::W16_TILE + row * 128;
           *reinterpret_cast<uint4*>(dst + (((2 * part) ^ (row & 7)) * 16)) = lo;
           *reinterpret_cast<uint4*>(dst + (((2 * part + 1) ^ (row & 7)) * 16)) = hi;
         }
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&conv[s]);
+      if (lane == 0) mbar_arrive(&conv[o]);
     }
     if (*abort_flag) raise_error(p.err, kDevTimeoutProducer);
   } else {
     // ------------------------------------------------------------ epilogue
-    const int et = threadIdx.x - 192;           // 0..127
+    const int et = threadIdx.x - C::EPI0;       // 0..127
     const int qq = warp & 3;                    // TMEM lane quarter of this warp
     const int f = qq * 32 + lane;               // weight row inside the tile
     const uint32_t lane_addr = (uint32_t)(qq * 32) << 16;
@@ -322,11 +363,11 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
             if (j >= tile.z) break;
             const size_t row = (size_t)(tile.y + j);
             if (KIND == 1) {
-              const float x1 = v[0][x], x2 = v[C::NW - 1][x];
+              const float x1 = v[0][x] * kAccUnscale, x2 = v[C::NW - 1][x] * kAccUnscale;
               const float cv = x2 * __frcp_rn(1.0f + __expf(-x2)) * x1;
               p.inter16[row * kInter + nt * 128 + f] = __float2half_rn(cv);
             } else {
-              p.down[row * kHidden + nt * 128 + f] = v[0][x];
+              p.down[row * kHidden + nt * 128 + f] = v[0][x] * kAccUnscale;
             }
           }
         }
@@ -351,21 +392,21 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
 // --------------------------------------------------------------------------
 // Host-side dispatch
 // --------------------------------------------------------------------------
-template <int KIND, int BN> struct B16Pick;
-template <> struct B16Pick<1, 64> { static constexpr int S = 4; };
-template <> struct B16Pick<1, 128> { static constexpr int S = 3; };
-template <> struct B16Pick<2, 64> { static constexpr int S = 4; };
-template <> struct B16Pick<2, 128> { static constexpr int S = 4; };
-template <> struct B16Pick<2, 256> { static constexpr int S = 3; };
+template <int KIND, int BN> struct B16Pick;   // raw stages RS, operand stages OS
+template <> struct B16Pick<1, 64> { static constexpr int RS = 6, OS = 2; };
+template <> struct B16Pick<1, 128> { static constexpr int RS = 5, OS = 2; };
+template <> struct B16Pick<2, 64> { static constexpr int RS = 8, OS = 3; };
+template <> struct B16Pick<2, 128> { static constexpr int RS = 6, OS = 3; };
+template <> struct B16Pick<2, 256> { static constexpr int RS = 4, OS = 3; };
 
 #define MOE_B16_CASES(X) X(1, 64) X(1, 128) X(2, 64) X(2, 128) X(2, 256)
 
 template <int KIND, int BN>
 static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
                                   int grid, cudaStream_t st) {
-  constexpr int S = B16Pick<KIND, BN>::S;
-  using C = B16Cfg<KIND, BN, S>;
-  auto kern = moe_gemm_f16_kernel<KIND, BN, S>;
+  using P = B16Pick<KIND, BN>;
+  using C = B16Cfg<KIND, BN, P::RS, P::OS>;
+  auto kern = moe_gemm_f16_kernel<KIND, BN, P::RS, P::OS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
@@ -373,7 +414,7 @@ static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm
 
 size_t gemm_f16_partials_bytes(int kind, int bn, int grid) {
 #define X(KD, BB) \
-  if (kind == KD && bn == BB) return (size_t)grid * 2 * B16Cfg<KD, BB, 1>::NW * BB * 128 * sizeof(float);
+  if (kind == KD && bn == BB) return (size_t)grid * 2 * B16Cfg<KD, BB, 1, 1>::NW * BB * 128 * sizeof(float);
   MOE_B16_CASES(X)
 #undef X
   return 0;
