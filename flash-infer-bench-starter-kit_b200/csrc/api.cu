@@ -30,7 +30,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
 int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
-constexpr int kWideMinTokens = 6144;
+constexpr int kWideMinTokens = 2560;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -75,6 +75,7 @@ int pick_bn(int T, int E_l) {
 struct Plan {
   moe_fp8_ds_layout pub;
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
+  int bt1, bt2;                     // compiled tile width of each GEMM (>= bn: the tile cap)
   bool wide;                        // large batch: f16-operand GEMMs (gemm_f16.cu)
   uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2;
 };
@@ -91,18 +92,36 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  // f16-operand GEMMs win once experts see ~190+ tokens each (measured on
-  // B200 with 32 local experts: 10% slower at T=4096, 7% faster at T=8192).
+  // f16-operand GEMMs win once experts see ~80+ tokens each (measured on B200
+  // with 32 local experts: even at T=2048, 7% faster at 3072, 15% at 4096).
   P->wide = g_path_override == 2 || (g_path_override == 0 && T >= kWideMinTokens);
   if (P->wide) {
-    // f16 kernels accumulate in TMEM, so tiles are as wide as TMEM allows:
-    // GEMM1 up to 128 tokens (X1 and X2), GEMM2 up to 256.
-    const double per_expert = (double)T * kTopK / kExpertsGlobal;
-    P->bn1 = per_expert > 64.0 ? 128 : 64;
-    P->bn2 = per_expert > 128.0 ? 256 : per_expert > 64.0 ? 128 : 64;
+    // f16 kernels accumulate in TMEM, so one tile takes up to 256 tokens.
+    // Wide tiles matter most: every weight byte a CTA converts then serves
+    // more tokens (measured on B200 at T=8192: GEMM1 with 128-token tiles
+    // 712 us, 112: 771, 80: 916).  The cap is also the token box height, so
+    // it follows the expected rows per expert (plus 30% for routing
+    // imbalance) where that is smaller.  GEMM1 tiles wider than 128 leave room
+    // for one TMEM accumulator only (X1 and X2), so its epilogue no longer
+    // overlaps the next tile; that pays only from ~384 rows per expert.
+    const double per_expert = 1.3 * (double)T * kTopK / kExpertsGlobal;
+    auto cap_for = [&](int widest) {
+      const int bn = ((int)ceil(per_expert) + 15) / 16 * 16;
+      return bn < 16 ? 16 : bn > widest ? widest : bn;
+    };
+    const int bn = cap_for(per_expert > 1.3 * 384.0 ? 256 : 128);
+    const int bn_2 = cap_for(256);
+    P->bn1 = g_bn_override[0] ? g_bn_override[0] : bn;
+    P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_2;
+    P->bt1 = P->bn1 > 128 ? 256 : 128;
+    P->bt2 = P->bn2 > 128 ? 256 : 128;
   } else {
-    P->bn1 = g_bn_override[0] ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
-    P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_auto;
+    // e4m3 kernels are compiled for 16, 32, 64 and 128 tokens only.
+    auto compiled = [](int v) { return v == 16 || v == 32 || v == 64 || v == 128; };
+    P->bn1 = compiled(g_bn_override[0]) ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
+    P->bn2 = compiled(g_bn_override[1]) ? g_bn_override[1] : bn_auto;
+    P->bt1 = P->bn1;
+    P->bt2 = P->bn2;
   }
 
   auto max_mt = [&](int bn) {
@@ -139,8 +158,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.down = take(R * kHidden * 4);
   if (P->wide) {
     P->grid1 = P->grid2 = sm_count;
-    P->partials1 = take(gemm_f16_partials_bytes(1, P->bn1, P->grid1));
-    P->partials2 = take(gemm_f16_partials_bytes(2, P->bn2, P->grid2));
+    P->partials1 = take(gemm_f16_partials_bytes(1, P->bt1, P->grid1));
+    P->partials2 = take(gemm_f16_partials_bytes(2, P->bt2, P->grid2));
   } else {
     P->grid1 = sm_count * gemm_ctas_per_sm(1, P->bn1);   // persistent: every resident CTA slot
     P->grid2 = sm_count * gemm_ctas_per_sm(2, P->bn2);
@@ -302,7 +321,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
   g1.inter16 = inter16;
-  ce = P.wide ? launch_gemm_f16(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s)
+  g1.box_rows = P.bn1;
+  ce = P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
               : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
@@ -314,7 +334,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
   g2.inter16 = nullptr;
-  ce = P.wide ? launch_gemm_f16(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s)
+  g2.box_rows = P.bn2;
+  ce = P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
               : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
@@ -419,7 +440,7 @@ const char* moe_fp8_ds_status_string(int status) {
 }
 
 int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2) {
-  auto ok = [](int v) { return v == 0 || v == 16 || v == 32 || v == 64 || v == 128; };
+  auto ok = [](int v) { return v >= 0 && v <= 256 && v % 16 == 0; };
   if (!ok(bn_gemm1) || !ok(bn_gemm2)) return MOE_ERR_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lk(g_mu);
   g_bn_override[0] = bn_gemm1;

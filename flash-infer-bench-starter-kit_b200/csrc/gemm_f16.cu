@@ -84,7 +84,10 @@ struct B16Cfg {
   static constexpr int OPS = NW * W16_TILE;                 // operand stage bytes
   static constexpr int OFF_OP = RS * RAW;                   // operand ring after the raw ring
   static constexpr int ACC = NW * BN;                       // TMEM columns of one tile accumulator
-  static constexpr int TMEM_COLS = 2 * ACC <= 128 ? 128 : 2 * ACC <= 256 ? 256 : 512;
+  // Two accumulators (the epilogue of one tile overlaps the next tile's MMAs)
+  // when they fit in TMEM's 512 columns, else one.
+  static constexpr int NACC = 2 * ACC <= 512 ? 2 : 1;
+  static constexpr int TMEM_COLS = NACC * ACC <= 128 ? 128 : NACC * ACC <= 256 ? 256 : 512;
   static constexpr int NCONV = MOE_F16_NCONV;               // converter warps
   static constexpr int EPI0 = 64 + 32 * NCONV;              // first epilogue thread
   static constexpr int THREADS = EPI0 + 128;
@@ -92,7 +95,7 @@ struct B16Cfg {
   static_assert(CROWS % 8 == 0, "converter rows");
   static constexpr int SMEM = 1024 + RS * RAW + OS * OPS + 1024;
   static_assert(RAW % 1024 == 0 && OPS % 1024 == 0, "1024-byte aligned stages");
-  static_assert(2 * ACC <= 512, "two TMEM accumulators");
+  static_assert(ACC <= 512, "TMEM accumulator");
   static_assert(BN % 16 == 0 && BN <= 256, "MMA N");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -174,7 +177,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         const int4 tile = p.tiles[mt];
         const int s = i % RS;
         if (!mbar_wait_bounded(&empty[s], ((i / RS) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], C::RAW);
+        mbar_arrive_expect_tx(&full[s], C::OFF_B + p.box_rows * 128);
         uint8_t* st = smem + s * C::RAW;
         // weights: e4m3 [rows][64 B] per tile (X1 then X2 for GEMM1)
         tma_load_3d(&tm_w, &full[s], st, 0, a, tile.x * C::W_ROWS + nt * 128, pol_w);
@@ -205,13 +208,13 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         sch.at(i, C::ATOMS, u, a, r);
         const bool seg_first = (i == sch.n1) || (a == 0);
         const bool seg_last = (a == C::ATOMS - 1) || (i == n_iter - 1);
-        const int b = seg & 1;
+        const int b = seg % C::NACC;
         if (seg_first) {   // MMA N covers the tile's rows only
           const int rows = p.tiles[unit_tile(u, sch.n_mt, C::NT).x].z;
           idesc = make_idesc_f16(128, min(BN, (rows + 15) & ~15));
         }
         if (seg_first &&
-            !mbar_wait_bounded(&acce[b], ((seg >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+            !mbar_wait_bounded(&acce[b], ((seg / C::NACC) & 1) ^ 1, abort_flag)) { ok = false; break; }
         // The converters waited for raw stage s before writing operand stage o,
         // so conv[o] also orders the token tile's TMA writes before the MMA.
         const int s = i % RS, o = i % OS;
@@ -299,8 +302,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       const int2 mn = unit_tile(u, sch.n_mt, C::NT);
       const int mt = mn.x, nt = mn.y;
       const int4 tile = p.tiles[mt];
-      const int b = seg & 1;
-      const bool got = mbar_wait_bounded(&accf[b], (seg >> 1) & 1, abort_flag);
+      const int b = seg % C::NACC;
+      const bool got = mbar_wait_bounded(&accf[b], (seg / C::NACC) & 1, abort_flag);
       if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
       tc_fence_after();
       const uint32_t acc0 = tmem_base + lane_addr + (uint32_t)(b * C::ACC);
@@ -393,13 +396,12 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
 // Host-side dispatch
 // --------------------------------------------------------------------------
 template <int KIND, int BN> struct B16Pick;   // raw stages RS, operand stages OS
-template <> struct B16Pick<1, 64> { static constexpr int RS = 6, OS = 2; };
 template <> struct B16Pick<1, 128> { static constexpr int RS = 5, OS = 2; };
-template <> struct B16Pick<2, 64> { static constexpr int RS = 8, OS = 3; };
+template <> struct B16Pick<1, 256> { static constexpr int RS = 3, OS = 2; };
 template <> struct B16Pick<2, 128> { static constexpr int RS = 6, OS = 3; };
 template <> struct B16Pick<2, 256> { static constexpr int RS = 4, OS = 3; };
 
-#define MOE_B16_CASES(X) X(1, 64) X(1, 128) X(2, 64) X(2, 128) X(2, 256)
+#define MOE_B16_CASES(X) X(1, 128) X(1, 256) X(2, 128) X(2, 256)
 
 template <int KIND, int BN>
 static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,

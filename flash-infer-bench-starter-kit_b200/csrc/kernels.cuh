@@ -15,6 +15,7 @@ struct GemmParams {
   int* ready;                 // per local expert: GEMM1 units finished (GEMM1 adds, GEMM2 waits)
   const int32_t* seg;         // per-expert row offsets (GEMM2: rows of expert e)
   int bn_prev;                // GEMM2: GEMM1's token-tile width
+  int box_rows;               // f16 GEMMs: rows of the token operand's TMA box (the tile cap)
   int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048]
