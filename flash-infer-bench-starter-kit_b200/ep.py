@@ -19,8 +19,10 @@ batch of tokens:
 Rows are ordered by (destination rank, token) and the combine sums in a fixed
 rank order, so the result is deterministic.  The exchange uses
 ``torch.distributed`` collectives (NCCL over NVLink on GPUs, gloo on CPU for
-the protocol tests); the per-rank compute is injected, so the same protocol
-code runs with the CUDA library on GPUs and with the CPU oracle in tests.
+the protocol tests).  The per-rank compute and the plan/pack/unpack/combine
+steps are injected: ``from_library`` runs all of them as kernels of
+libmoe_fp8_ds.so, the protocol tests run the PyTorch statement of the same
+steps (``TorchPlumbing``) with the CPU oracle.
 """
 
 from __future__ import annotations
@@ -33,12 +35,11 @@ SCALE_BYTES = (H // 128) * 4                    # 56 fp32 scales per row
 ROW_BYTES = H + SCALE_BYTES + TOP_K * 4 + TOP_K * 4   # hidden | scales | ids | weights = 7456
 
 
-def pack_rows(ids, w, hidden, hidden_scale, world, E_l):
-    """Build the dispatch rows.
+def plan_rows(ids, world, E_l):
+    """Dispatch plan: ``(counts [world] int64, slot [T, world] int64, src_token [S] int64)``.
 
-    Returns ``(send [S, ROW_BYTES] uint8, counts [world] int64, src_token [S] int64,
-    slot [T, world] int64)``: rows grouped by destination rank, tokens ascending
-    inside a group; ``slot[t, r]`` is the row of token t sent to rank r, or -1.
+    Rows are grouped by destination rank, tokens ascending inside a group;
+    ``slot[t, r]`` is the send row of token t for rank r, or -1.
     """
     T = ids.shape[0]
     dev = ids.device
@@ -50,14 +51,24 @@ def pack_rows(ids, w, hidden, hidden_scale, world, E_l):
     src_token = rt[:, 1]
     slot = torch.full((T, world), -1, dtype=torch.long, device=dev)
     slot[rt[:, 1], rt[:, 0]] = torch.arange(rt.shape[0], device=dev)
+    return counts, slot, src_token
+
+
+def gather_rows(ids, w, hidden, hidden_scale, src_token):
+    """Send rows ``[S, ROW_BYTES]`` uint8 for the tokens ``src_token``."""
     scale_rows = hidden_scale.t()                               # [T, 56] view
-    send = torch.cat([
+    return torch.cat([
         hidden.view(torch.uint8).index_select(0, src_token),
         scale_rows.index_select(0, src_token).contiguous().view(torch.uint8),
         ids.to(torch.int32).index_select(0, src_token).contiguous().view(torch.uint8),
         w.to(torch.float32).index_select(0, src_token).contiguous().view(torch.uint8),
     ], dim=1)
-    return send, counts, src_token, slot
+
+
+def pack_rows(ids, w, hidden, hidden_scale, world, E_l):
+    """``(send [S, ROW_BYTES] uint8, counts, src_token, slot)``, see ``plan_rows``."""
+    counts, slot, src_token = plan_rows(ids, world, E_l)
+    return gather_rows(ids, w, hidden, hidden_scale, src_token), counts, src_token, slot
 
 
 def unpack_rows(recv):
@@ -72,10 +83,10 @@ def unpack_rows(recv):
 
 
 def combine_rows(back, slot, T):
-    """out[t] = sum over ranks r ascending of back[slot[t, r]] (fp32)."""
+    """out[t] = sum over ranks r ascending of back[slot[t, r]] (fp32, from +0)."""
     acc = torch.zeros(T, H, dtype=torch.float32, device=back.device)
     for r in range(slot.shape[1]):
-        s = slot[:, r]
+        s = slot[:, r].long()
         has = s >= 0
         if bool(has.any()):
             rows = back.index_select(0, s.clamp_min(0)).float()
@@ -83,17 +94,77 @@ def combine_rows(back, slot, T):
     return acc
 
 
-def exchange(send, counts, group=None):
-    """Count exchange then variable-size row all-to-all.  Returns (recv, in_splits, out_splits)."""
-    world = dist.get_world_size(group)
-    recv_counts = torch.empty_like(counts)
-    dist.all_to_all_single(recv_counts, counts, group=group)
-    in_splits = counts.tolist()
-    out_splits = recv_counts.tolist()
-    recv = torch.empty(sum(out_splits), send.shape[1], dtype=send.dtype, device=send.device)
-    dist.all_to_all_single(recv, send, out_splits, in_splits, group=group)
-    del world
-    return recv, in_splits, out_splits
+class TorchPlumbing:
+    """Plan/pack/unpack/combine in PyTorch: the protocol on CPU (gloo tests)
+    and the checker the library's kernels are tested against."""
+
+    def plan(self, ids, world, E_l):
+        return plan_rows(ids, world, E_l)
+
+    def pack(self, ids, w, hidden, hidden_scale, src_token, rows):
+        return gather_rows(ids, w, hidden, hidden_scale, src_token[:rows].long())
+
+    def unpack(self, recv):
+        return unpack_rows(recv)
+
+    def combine(self, back, slot, T, output):
+        output.copy_(combine_rows(back, slot, T).to(output.dtype))
+
+
+class LibPlumbing:
+    """The same steps as kernels of libmoe_fp8_ds.so (``moe_fp8_ds_ep_*``),
+    one launch each, bit-identical to ``TorchPlumbing``."""
+
+    def __init__(self):
+        import ctypes
+        from . import _lib
+        self._c = ctypes
+        self._L = _lib
+        self._lib = _lib.load()
+
+    def _p(self, t):
+        return self._c.c_void_p(t.data_ptr() if t is not None and t.numel() else 0)
+
+    def _s(self, dev):
+        return self._c.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+    def plan(self, ids, world, E_l):
+        T, dev = ids.shape[0], ids.device
+        ids = ids.to(torch.int32).contiguous()
+        counts = torch.empty(world, dtype=torch.int64, device=dev)
+        slot = torch.empty(T, world, dtype=torch.int32, device=dev)
+        src = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
+        self._L.check(self._lib.moe_fp8_ds_ep_plan(self._p(ids), T, world, E_l, self._p(counts), self._p(slot),
+                                                   self._p(src), self._s(dev)), "moe_fp8_ds_ep_plan")
+        return counts, slot, src
+
+    def pack(self, ids, w, hidden, hidden_scale, src_token, rows):
+        dev = hidden.device
+        send = torch.empty(rows, ROW_BYTES, dtype=torch.uint8, device=dev)
+        ids = ids.to(torch.int32).contiguous()
+        w = w.to(torch.float32).contiguous()
+        self._L.check(self._lib.moe_fp8_ds_ep_pack(self._p(ids), self._p(w), self._p(hidden), self._p(hidden_scale),
+                                                   hidden.shape[0], self._p(src_token), rows, self._p(send),
+                                                   self._s(dev)), "moe_fp8_ds_ep_pack")
+        return send
+
+    def unpack(self, recv):
+        R, dev = recv.shape[0], recv.device
+        hidden = torch.empty(R, H, dtype=torch.float8_e4m3fn, device=dev)
+        scale = torch.empty(H // 128, R, dtype=torch.float32, device=dev)
+        ids = torch.empty(R, TOP_K, dtype=torch.int32, device=dev)
+        w = torch.empty(R, TOP_K, dtype=torch.float32, device=dev)
+        self._L.check(self._lib.moe_fp8_ds_ep_unpack(self._p(recv), R, self._p(hidden), self._p(scale),
+                                                     self._p(ids), self._p(w), self._s(dev)), "moe_fp8_ds_ep_unpack")
+        return hidden, scale, ids, w
+
+    def combine(self, back, slot, T, output):
+        if back.dtype != torch.bfloat16 or output.dtype != torch.bfloat16 or not output.is_contiguous():
+            raise TypeError("the library combine takes bf16 partials and a contiguous bf16 output")
+        slot = slot.to(torch.int32).contiguous()
+        self._L.check(self._lib.moe_fp8_ds_ep_combine(self._p(back), self._p(slot), T, slot.shape[1],
+                                                      self._p(output), self._s(output.device)),
+                      "moe_fp8_ds_ep_combine")
 
 
 class ExpertParallelMoE:
@@ -101,13 +172,15 @@ class ExpertParallelMoE:
 
     ``route_fn(logits, bias, scale) -> (ids int32 [T,8] ascending, w fp32 [T,8])`` and
     ``expert_fn(ids, w, hidden, hidden_scale, w13, s13, w2, s2, offset) -> partial [R, H]``
-    supply the per-rank compute; ``from_library`` wires the CUDA library.
+    supply the per-rank compute, ``plumbing`` the plan/pack/unpack/combine
+    steps; ``from_library`` wires the CUDA library for all of them.
     """
 
-    def __init__(self, route_fn, expert_fn, group=None):
+    def __init__(self, route_fn, expert_fn, group=None, plumbing=None):
         self.route_fn = route_fn
         self.expert_fn = expert_fn
         self.group = group
+        self.plumbing = plumbing if plumbing is not None else TorchPlumbing()
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         if E_GLOBAL % self.world:
@@ -122,25 +195,30 @@ class ExpertParallelMoE:
         if gemm1_weights.shape[0] != self.E_l:
             raise ValueError(f"rank holds {gemm1_weights.shape[0]} experts, expected {self.E_l}")
         T = hidden_states.shape[0]
+        pl = self.plumbing
         ids, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
-        send, counts, src_token, slot = pack_rows(ids, w, hidden_states, hidden_states_scale,
-                                                  self.world, self.E_l)
-        recv, in_splits, out_splits = exchange(send, counts, self.group)
-        r_hidden, r_scale, r_ids, r_w = unpack_rows(recv)
+        counts, slot, src_token = pl.plan(ids, self.world, self.E_l)
+        # count exchange, then the row all-to-all moves only real rows
+        recv_counts = torch.empty_like(counts)
+        dist.all_to_all_single(recv_counts, counts, group=self.group)
+        in_splits, out_splits = counts.tolist(), recv_counts.tolist()
+        send = pl.pack(ids, w, hidden_states, hidden_states_scale, src_token, sum(in_splits))
+        recv = torch.empty(sum(out_splits), ROW_BYTES, dtype=torch.uint8, device=send.device)
+        dist.all_to_all_single(recv, send, out_splits, in_splits, group=self.group)
+        r_hidden, r_scale, r_ids, r_w = pl.unpack(recv)
         part = self.expert_fn(r_ids, r_w, r_hidden, r_scale, gemm1_weights, gemm1_weights_scale,
                               gemm2_weights, gemm2_weights_scale, self.rank * self.E_l)
         back = torch.empty(send.shape[0], H, dtype=part.dtype, device=part.device)
         dist.all_to_all_single(back, part, in_splits, out_splits, group=self.group)
-        acc = combine_rows(back, slot, T)
-        output.copy_(acc.to(output.dtype))
+        pl.combine(back, slot, T, output)
         self.last_stats = {"sent_rows": int(send.shape[0]), "recv_rows": int(recv.shape[0])}
         return output
 
     __call__ = forward
 
 
-def from_library(group=None, partial_dtype=torch.bfloat16):
-    """ExpertParallelMoE whose routing and expert compute run in libmoe_fp8_ds.so."""
+def from_library(group=None):
+    """ExpertParallelMoE whose routing, plumbing and expert compute run in libmoe_fp8_ds.so."""
     import ctypes
     import importlib
     from . import _lib
@@ -159,17 +237,12 @@ def from_library(group=None, partial_dtype=torch.bfloat16):
 
     def expert_fn(ids, w, hidden, scale, w13, s13, w2, s2, offset):
         R = hidden.shape[0]
-        if partial_dtype == torch.float32:
-            out = torch.empty(R, H, dtype=torch.float32, device=hidden.device)
-            args = K.build_args(None, None, hidden, scale, w13, s13, w2, s2, offset, 1.0, None,
-                                topk_ids=ids, topk_weights=w, output_f32=out)
-        else:
-            out = torch.empty(R, H, dtype=torch.bfloat16, device=hidden.device)
-            args = K.build_args(None, None, hidden, scale, w13, s13, w2, s2, offset, 1.0, out,
-                                topk_ids=ids, topk_weights=w)
+        out = torch.empty(R, H, dtype=torch.bfloat16, device=hidden.device)
+        args = K.build_args(None, None, hidden, scale, w13, s13, w2, s2, offset, 1.0, out,
+                            topk_ids=ids, topk_weights=w)
         if R:
             ws = K.get_workspace(hidden.device, K.workspace_bytes(R, w13.shape[0]))
             K.run_with_workspace(args, ws, routed=True)
         return out
 
-    return ExpertParallelMoE(route_fn, expert_fn, group)
+    return ExpertParallelMoE(route_fn, expert_fn, group, plumbing=LibPlumbing())

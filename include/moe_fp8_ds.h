@@ -178,6 +178,40 @@ MOE_API int moe_fp8_ds_set_stage_events(void* const* events, int32_t count);
  * share one launch; 6 above; moe_fp8_ds_run_routed always enqueues 6). */
 MOE_API int moe_fp8_ds_launches_per_call(int32_t num_tokens);
 
+/* ---------------------------------------------------------------------------
+ * Expert-parallel plumbing (no counterpart in the reference, whose only
+ * multi-GPU hook is local_expert_offset, solution/python/kernel.py:104).
+ * Rank r of `world` owns global experts [r*E_r, (r+1)*E_r), E_r*world = 256.
+ * A dispatch row is hidden e4m3 [7168] | scales fp32 [56] | ids int32 [8] |
+ * weights fp32 [8] = 7456 bytes; rows go to ranks in (rank, token) order.
+ * ------------------------------------------------------------------------- */
+#define MOE_EP_ROW_BYTES 7456
+
+/* From the routing (topk_ids [T,8]): rows per destination rank (counts, int64
+ * [world]), the send row of each (token, rank) pair or -1 (slot, int32
+ * [T, world]) and the source token of each send row (src_token, int32, at
+ * least T*world entries; the first sum(counts) are written).  world <= 8.   */
+MOE_API int moe_fp8_ds_ep_plan(const int32_t* topk_ids, int32_t num_tokens, int32_t world,
+                               int32_t experts_per_rank, int64_t* counts, int32_t* slot,
+                               int32_t* src_token, void* stream);
+
+/* Build `rows` dispatch rows (send, [rows, 7456] bytes) from src_token.     */
+MOE_API int moe_fp8_ds_ep_pack(const int32_t* topk_ids, const float* topk_weights, const void* hidden_states,
+                               const float* hidden_states_scale, int32_t num_tokens, const int32_t* src_token,
+                               int32_t rows, void* send, void* stream);
+
+/* Split received rows into the layer's argument layout: hidden e4m3
+ * [rows, 7168], scales fp32 [56, rows], ids int32 [rows, 8], weights fp32
+ * [rows, 8] (the inputs of moe_fp8_ds_run_routed).                          */
+MOE_API int moe_fp8_ds_ep_unpack(const void* recv, int32_t rows, void* hidden_states, float* hidden_states_scale,
+                                 int32_t* topk_ids, float* topk_weights, void* stream);
+
+/* output[t] = bf16(sum over ranks r ascending with slot[t][r] >= 0 of
+ * partials[slot[t][r]]), the sum in fp32 from +0; partials bf16 [S, 7168]
+ * in send-row order, output bf16 [T, 7168].                                 */
+MOE_API int moe_fp8_ds_ep_combine(const void* partials, const int32_t* slot, int32_t num_tokens, int32_t world,
+                                  void* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -66,6 +66,17 @@ def test_argument_validation_without_gpu(pkg):
     a.num_tokens = 4
     assert lib.moe_fp8_ds_run(ctypes.byref(a), None, 0, None) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_tile_override(24, 0) == L.MOE_ERR_INVALID_ARGUMENT
+    # expert-parallel plumbing: shapes are checked before any launch
+    cnt = ctypes.c_void_p(16)
+    assert lib.moe_fp8_ds_ep_plan(None, 0, 3, 85, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_plan(None, 0, 2, 64, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_plan(None, 0, 16, 16, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_plan(None, 4, 2, 128, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_pack(None, None, None, None, 4, None, 0, None, None) == L.MOE_OK
+    assert lib.moe_fp8_ds_ep_pack(None, None, None, None, 4, None, 2, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_unpack(None, 0, None, None, None, None, None) == L.MOE_OK
+    assert lib.moe_fp8_ds_ep_combine(None, None, 0, 2, None, None) == L.MOE_OK
+    assert lib.moe_fp8_ds_ep_combine(None, None, 4, 9, None, None) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_tile_override(0, 0) == L.MOE_OK
 
 
