@@ -68,6 +68,22 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
+def measured_tensor_peak():
+    """Dense bf16/f16 tensor peak (TFLOP/s, burst: the GEMMs are timed alone)."""
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return float(d["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
+
+
+WIDE_MIN_TOKENS = 2560      # the library switches to the f16-operand GEMMs here (api.cu)
+
+
+def workload_name(T, E_l):
+    return f"{'decode' if T <= 256 else 'prefill'}_T{T}_E{E_l}"
+
+
 # ---------------------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi sampling (200 ms) while the timed region runs."""
@@ -252,7 +268,7 @@ def run_reference_arm(a, T, E_l):
         "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt * 1e3,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic",
-        "config": {"workload": f"decode_T{T}_E{E_l}", "tokens": T, "local_experts": E_l,
+        "config": {"workload": workload_name(T, E_l), "tokens": T, "local_experts": E_l,
                    "note": "reference CPU path (oracle port of solution/cuda/moe.cu:137-240, fp32 on host cores)"},
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
                          "sample": f"{a.steps} full layer calls at T={T}, E_l={E_l}"},
@@ -456,7 +472,20 @@ def main():
         cpu = {"value": T / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} full layer call(s) at T={T}, E_l={E_l} (fp32 oracle port, {sec:.2f} s/call)"}
 
-    workload = f"decode_T{T}_E{E_l}"
+    workload = workload_name(T, E_l)
+    if T >= WIDE_MIN_TOKENS:
+        # f16-operand GEMMs: bound by the tensor pipe (dense f16 = bf16 rate)
+        t_peak, t_kind = measured_tensor_peak()
+        flops = R * (2 * H * 2 * I if dom == "gemm1" else 2 * I * H)
+        t_ach = flops / (stages[dom] * 1e-3) / 1e12
+        roof = {"kernel": dom, "bound": "tensor", "achieved": t_ach, "peak": t_peak, "unit": "TFLOP/s",
+                "frac": t_ach / t_peak, "peak_kind": t_kind, "algorithmic_flops": flops,
+                "kernel_ms": stages[dom], "traffic": traffic_from_profile(workload, dom)}
+    else:
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                "frac": achieved / hbm_peak, "peak_kind": peak_kind,
+                "algorithmic_bytes": ab[dom], "kernel_ms": stages[dom],
+                "traffic": traffic_from_profile(workload, dom)}
     line = {
         "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
@@ -468,10 +497,7 @@ def main():
                    "layer_hbm_gbs": ab["layer"] / (ms * 1e-3) / 1e9,
                    "layer_hbm_frac": ab["layer"] / (ms * 1e-3) / 1e9 / hbm_peak,
                    "us_per_call": ms * 1e3},
-        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": achieved / hbm_peak, "peak_kind": peak_kind,
-                     "algorithmic_bytes": ab[dom], "kernel_ms": stages[dom],
-                     "traffic": traffic_from_profile(workload, dom)},
+        "roofline": roof,
         "stage_ms": stages,
         "sweep": sweep,
         "cpu_baseline": cpu,
