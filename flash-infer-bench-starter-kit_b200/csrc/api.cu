@@ -358,6 +358,21 @@ int run_layer_with_workspace(const moe_fp8_ds_args* a, void* ws, uint64_t ws_byt
 
 using namespace moe;
 
+namespace moe {
+// Failure-detection self test: one thread waits, with the bounded wait every
+// pipeline wait uses, on a counter nothing increments (word 3 of the
+// workspace's error block, zeroed by the host first).  When the wait gives up
+// it records kDevTimeoutBarrier in the error word and the kernel returns, so
+// the context stays usable.
+__global__ void selftest_wait_kernel(int* words) {
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    if (!wait_counter(words + 3, 1, &abort_flag)) raise_error(words, kDevTimeoutBarrier);
+  }
+}
+}  // namespace moe
+
 extern "C" {
 
 int moe_fp8_ds_workspace_layout(int32_t num_tokens, int32_t num_local_experts,
@@ -407,6 +422,19 @@ int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int3
                                 routed_scaling_factor, 0, 0, topk_ids, topk_weights, nullptr, 0,
                                 nullptr, static_cast<cudaStream_t>(stream));
   return ce == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
+}
+
+int moe_fp8_ds_selftest_wait_timeout(void* workspace, void* stream) {
+  if (!workspace) return MOE_ERR_INVALID_ARGUMENT;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOE_ERR_MISALIGNED;
+  DeviceInfo di;
+  const int st = device_info(&di);
+  if (st != MOE_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int* words = static_cast<int*>(workspace);
+  if (cudaMemsetAsync(words + 3, 0, 4, s) != cudaSuccess) return MOE_ERR_CUDA;
+  moe::selftest_wait_kernel<<<1, 32, 0, s>>>(words);
+  return cudaGetLastError() == cudaSuccess ? MOE_OK : MOE_ERR_CUDA;
 }
 
 int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t* device_error) {

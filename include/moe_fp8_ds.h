@@ -149,6 +149,14 @@ MOE_API int moe_fp8_ds_route(const float* routing_logits, const void* routing_bi
  * to a moe_status.                                                         */
 MOE_API int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t* device_error);
 
+/* Failure-detection self test (no counterpart in the reference): enqueue a
+ * one-thread kernel that waits, with the layer's bounded device-side wait
+ * (about one second), on a workspace counter nothing increments.  The wait
+ * gives up, records a timeout in the workspace error word and returns; the
+ * next moe_fp8_ds_read_device_error reports MOE_ERR_DEVICE_TIMEOUT and the
+ * context stays usable.  Uses 16 bytes at the workspace base.              */
+MOE_API int moe_fp8_ds_selftest_wait_timeout(void* workspace, void* stream);
+
 /* Static description of a status code. */
 MOE_API const char* moe_fp8_ds_status_string(int status);
 

@@ -99,3 +99,59 @@ def test_ep_protocol_matches_single_process(world):
         assert det, f"rank {rank}: two calls differ"
         assert err <= 1e-2 * max(mx, 1e-6) + 1e-5, f"rank {rank}: error {err} vs max {mx}"
         assert stats["sent_rows"] > 0
+
+
+def _worker_dead_peer(rank, world, port, q):
+    """Rank 1 fails before the exchange (an exception on the host) and leaves;
+    rank 0 must get an error from its next collective, not hang."""
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    from oracle import moe_ref
+    ep_mod = __import__("fib_b200.ep", fromlist=["ep"])
+    E_l = 256 // world
+
+    def route_fn(logits, bias, scale):
+        ids, w, _ = moe_ref.route(logits, bias, scale)
+        return ids.to(torch.int32), w
+
+    def expert_fn(ids, w, hidden, scale, w13, s13, w2, s2, offset):
+        return standin_experts(ids, w, hidden, scale, w13, s13, w2, s2, offset, E_l)
+
+    layer = ep_mod.ExpertParallelMoE(route_fn, expert_fn)
+    logits, bias, hs, hss = pkg.inputs.make_token_inputs(8, seed=300 + rank)
+    dummy = torch.empty(E_l, 1)
+    out = torch.empty(8, H, dtype=torch.bfloat16)
+    def report(msg):
+        q.put(msg)
+        q.close()
+        q.join_thread()      # flush before the hard exit
+
+    if rank == 1:
+        report((rank, "left", 0.0))
+        os._exit(0)          # the rank dies between steps, with nothing in flight
+    t0 = time.monotonic()
+    try:
+        layer(logits, bias, hs, hss, dummy, dummy, dummy, dummy, 2.5, out)
+        report((rank, "no error", time.monotonic() - t0))
+    except Exception as e:  # noqa: BLE001  (any collective error is the expected outcome)
+        report((rank, "error:" + type(e).__name__, time.monotonic() - t0))
+    os._exit(0)
+
+
+def test_ep_dead_peer_raises_instead_of_hanging():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_dead_peer, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict((r[0], r[1:]) for r in (q.get(timeout=180) for _ in range(2)))
+    for p in procs:
+        p.join(timeout=60)
+    assert res[1][0] == "left"
+    assert res[0][0].startswith("error:"), res[0]
+    assert res[0][1] < 60.0, f"the surviving rank waited {res[0][1]:.1f} s"
