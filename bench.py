@@ -51,7 +51,10 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=20)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    p.add_argument("--impl", choices=("ours", "reference", "reference-gpu"), default="ours",
+                   help="reference: the reference's CPU path (oracle port) on the host cores; "
+                        "reference-gpu: the reference's own CUTLASS GPU pipeline, prebuilt by "
+                        "oracle/build_ref_gpu.py, timed on the same workloads (side comparison)")
     p.add_argument("--tokens", type=int, default=64, help="headline T")
     p.add_argument("--sweep", default="1,16,1024,4096", help="extra T values ('' for none)")
     p.add_argument("--local-experts", type=int, default=32)
@@ -391,6 +394,61 @@ def run_reference_arm_ep(a, world):
         "gpu_launches": 0}), flush=True)
 
 
+def run_reference_gpu_arm(a, T, E_l):
+    """Time the reference's own GPU solution (solution/python/kernel.py:95-120 ->
+    main.cpp run) on this arm's workloads, with the same L2 flush and event timing,
+    and report its output error next to ours against the CPU oracle."""
+    base_line = {"impl": "reference-gpu", "metric": "moe_layer_tokens_per_s", "unit": "tokens/s"}
+    if int(os.environ.get("WORLD_SIZE", "1")) > 1 or E_l != 32:
+        print(json.dumps({**base_line, "unavailable": "the reference GPU path is single-GPU with 32 local experts"}))
+        return
+    try:
+        from oracle import build_ref_gpu
+        mod = build_ref_gpu.load()
+    except Exception as e:  # noqa: BLE001
+        print(json.dumps({**base_line, "unavailable": f"reference GPU extension not built: {e}"}))
+        return
+    from oracle import moe_ref
+    pkg = graft.load_package()
+    dev = torch.device("cuda", 0)
+    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep not in ("", "none") else []
+    base_cpu = pkg.inputs.make_inputs(max([T] + sweep_T), E_l=E_l, seed=0)
+    base = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in base_cpu.items()}
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def timed(Tm, impl):
+        inp = token_slice(base, Tm)
+        out = torch.empty(Tm, H, dtype=torch.bfloat16, device=dev)
+        args = pkg.inputs.as_args(inp)
+        fn = (lambda: mod.run(*args, out)) if impl == "ref" else (lambda: pkg.kernel(*args, out))
+        ts = time_steps(fn, a.steps, a.warmup, flush)
+        return sum(ts) / len(ts), out
+
+    ms_ref, out_ref = timed(T, "ref")
+    ms_ours, out_ours = timed(T, "ours")
+    ref32 = moe_ref.moe_forward(*pkg.inputs.as_args(token_slice(base_cpu, T)), return_fp32=True)
+
+    def err(o):
+        d = (o.float().cpu() - ref32).abs()
+        return {"max_abs": float(d.max()), "mean_rel": float((d / ref32.abs().clamp_min(1e-2)).mean()),
+                "within_atol1e-2_rtol2e-2": float((d <= 1e-2 + 2e-2 * ref32.abs()).float().mean())}
+    sweep = []
+    for Ts in sweep_T:
+        mr, _ = timed(Ts, "ref")
+        mo, _ = timed(Ts, "ours")
+        sweep.append({"tokens": Ts, "reference_us": mr * 1e3, "ours_us": mo * 1e3, "speedup": mr / mo})
+    print(json.dumps({
+        **base_line, "value": T / (ms_ref * 1e-3), "ms_per_step": ms_ref, "n_gpus": 1, "steps": a.steps,
+        "warmup": a.warmup, "higher_is_better": True, "data": "synthetic",
+        "config": {"workload": workload_name(T, E_l), "tokens": T, "local_experts": E_l,
+                   "l2": "flushed (256 MiB write) before every timed step",
+                   "note": "reference CUTLASS pipeline (main.cpp run), prebuilt for sm_100a"},
+        "ours_ms_per_step": ms_ours, "speedup_ours_vs_reference": ms_ref / ms_ours,
+        "error_vs_oracle": {"reference": err(out_ref), "ours": err(out_ours)},
+        "sweep": sweep,
+    }), flush=True)
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -399,6 +457,11 @@ def main():
     E_l = a.local_experts
     T = a.tokens
 
+    if a.impl == "reference-gpu":
+        if rank == 0:
+            torch.cuda.set_device(0)
+            run_reference_gpu_arm(a, T, E_l)
+        return
     if a.impl == "reference":
         if rank == 0:
             if world > 1:

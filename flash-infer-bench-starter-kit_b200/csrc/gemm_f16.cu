@@ -40,12 +40,11 @@ namespace moe {
 #endif
 
 // Shared memory holds two rings:
-//   operand ring (OS stages): the converted f16 weight tile(s) the MMA reads;
-//   raw ring: what TMA writes -- the e4m3 weight tile(s) and the f16 token
-//     tile; a stage is free once the MMA that read its tokens is done.
-// Only the raw ring waits on memory latency, so it takes all the remaining
-// space: its stage holds the token box actually loaded (the tile cap, a run
-// time value), and its depth is as many such stages as fit (at most 8).
+//   raw ring (RS stages): what TMA writes -- the e4m3 weight tile(s) and the
+//     f16 token tile; a stage is free once the MMA that read its tokens is done;
+//   operand ring (OS stages): the converted f16 weight tile(s) the MMA reads.
+// Only the raw ring waits on memory latency, so it gets most of the space:
+// deeper prefetch for the same shared memory than one ring of whole stages.
 // Weight conversion: e4m3 -> f16 by cvt (exact), then one f16 multiply by
 // f16(s * 2^8), s the 128x128 block scale.  The 2^8 keeps small products out
 // of the f16 subnormal range; the epilogue multiplies the fp32 accumulator by
@@ -70,7 +69,7 @@ __device__ __forceinline__ void convert16(uint4 src, float scale, uint4& lo, uin
   hi = make_uint4(out[4], out[5], out[6], out[7]);
 }
 
-template <int KIND, int BN, int OS>
+template <int KIND, int BN, int RS, int OS>
 struct B16Cfg {
   static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles (X1, X2) per stage
   static constexpr int K = KIND == 1 ? kHidden : kInter;    // reduction length
@@ -79,13 +78,11 @@ struct B16Cfg {
   static constexpr int W_ROWS = KIND == 1 ? kGemm1Out : kHidden;
   static constexpr int W8_TILE = 128 * 64;                  // e4m3 staging: 128 rows x 64 B
   static constexpr int W16_TILE = 128 * 128;                // f16: 128 rows x 128 B (swizzled)
+  static constexpr int B_TILE = BN * 128;                   // f16 tokens: BN rows x 128 B
   static constexpr int OFF_B = NW * W8_TILE;               // token tile inside a raw stage
+  static constexpr int RAW = OFF_B + B_TILE;                // raw stage bytes
   static constexpr int OPS = NW * W16_TILE;                 // operand stage bytes
-  static constexpr int OFF_RAW = OS * OPS;                  // raw ring after the operand ring
-  static constexpr int MAX_RS = 8;
-  static constexpr int AUX = 1024;                          // barriers and flags
-  static constexpr int SMEM = 227 * 1024;                   // all of it: one CTA per SM
-  static constexpr int RING_BYTES = SMEM - 1024 - AUX - OFF_RAW;   // 1024: alignment slack
+  static constexpr int OFF_OP = RS * RAW;                   // operand ring after the raw ring
   static constexpr int ACC = NW * BN;                       // TMEM columns of one tile accumulator
   // Two accumulators (the epilogue of one tile overlaps the next tile's MMAs)
   // when they fit in TMEM's 512 columns, else one.
@@ -96,10 +93,11 @@ struct B16Cfg {
   static constexpr int THREADS = EPI0 + 128;
   static constexpr int CROWS = 128 / NCONV;                 // weight rows per converter warp
   static_assert(CROWS % 8 == 0, "converter rows");
-  static_assert(OFF_B % 1024 == 0 && OPS % 1024 == 0, "1024-byte aligned stages");
+  static constexpr int SMEM = 1024 + RS * RAW + OS * OPS + 1024;
+  static_assert(RAW % 1024 == 0 && OPS % 1024 == 0, "1024-byte aligned stages");
   static_assert(ACC <= 512, "TMEM accumulator");
   static_assert(BN % 16 == 0 && BN <= 256, "MMA N");
-  static_assert(RING_BYTES >= 2 * (OFF_B + BN * 128), "two raw stages of the widest box");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
 // Instruction descriptor for kind::f16: A = B = f16, D = f32, K-major, M = 128.
@@ -121,21 +119,17 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-template <int KIND, int BN, int OS>
-__global__ void __launch_bounds__(B16Cfg<KIND, BN, OS>::THREADS, 1)
+template <int KIND, int BN, int RS, int OS>
+__global__ void __launch_bounds__(B16Cfg<KIND, BN, RS, OS>::THREADS, 1)
 moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_b,
                      const GemmParams p) {
-  using C = B16Cfg<KIND, BN, OS>;
+  using C = B16Cfg<KIND, BN, RS, OS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  // raw stage: weight tile(s), then box_rows token rows (a multiple of 16 rows = 2 KB)
-  const int raw_bytes = C::OFF_B + p.box_rows * 128;
-  const int raw_stride = (raw_bytes + 1023) & ~1023;
-  const int RS = min(C::MAX_RS, C::RING_BYTES / raw_stride);
-  uint8_t* aux = smem + C::OFF_RAW + C::RING_BYTES;
+  uint8_t* aux = smem + C::OFF_OP + OS * C::OPS;
   uint64_t* full = reinterpret_cast<uint64_t*>(aux);       // TMA bytes of raw stage s landed
-  uint64_t* empty = full + C::MAX_RS;                       // MMA finished with raw stage s
-  uint64_t* conv = empty + C::MAX_RS;                       // converters wrote operand stage o
+  uint64_t* empty = full + RS;                              // MMA finished with raw stage s
+  uint64_t* conv = empty + RS;                              // converters wrote operand stage o
   uint64_t* opempty = conv + OS;                            // MMA finished with operand stage o
   uint64_t* accf = opempty + OS;                            // accumulator b complete
   uint64_t* acce = accf + 2;                                // accumulator b drained
@@ -183,8 +177,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         const int4 tile = p.tiles[mt];
         const int s = i % RS;
         if (!mbar_wait_bounded(&empty[s], ((i / RS) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], raw_bytes);
-        uint8_t* st = smem + C::OFF_RAW + s * raw_stride;
+        mbar_arrive_expect_tx(&full[s], C::OFF_B + p.box_rows * 128);
+        uint8_t* st = smem + s * C::RAW;
         // weights: e4m3 [rows][64 B] per tile (X1 then X2 for GEMM1)
         tma_load_3d(&tm_w, &full[s], st, 0, a, tile.x * C::W_ROWS + nt * 128, pol_w);
         if (KIND == 1)
@@ -226,8 +220,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         const int s = i % RS, o = i % OS;
         if (!mbar_wait_bounded(&conv[o], (i / OS) & 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
-        const uint64_t bdesc = make_sdesc_sw128(smem_base + C::OFF_RAW + s * raw_stride + C::OFF_B);
-        const uint32_t op = smem_base + o * C::OPS;
+        const uint64_t bdesc = make_sdesc_sw128(smem_base + s * C::RAW + C::OFF_B);
+        const uint32_t op = smem_base + C::OFF_OP + o * C::OPS;
 #pragma unroll
         for (int w = 0; w < C::NW; ++w) {
           const uint64_t adesc = make_sdesc_sw128(op + w * C::W16_TILE);
@@ -265,8 +259,8 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       }
       if (!mbar_wait_bounded(&full[s], (i / RS) & 1, abort_flag)) break;
       if (!mbar_wait_bounded(&opempty[o], ((i / OS) & 1) ^ 1, abort_flag)) break;
-      const uint8_t* st = smem + C::OFF_RAW + s * raw_stride;
-      uint8_t* opst = smem + o * C::OPS;
+      const uint8_t* st = smem + s * C::RAW;
+      uint8_t* opst = smem + C::OFF_OP + o * C::OPS;
       const int part = lane & 3;
 #pragma unroll
       for (int w = 0; w < C::NW * (MOE_F16_PROBE != 1); ++w) {
@@ -401,11 +395,11 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
 // --------------------------------------------------------------------------
 // Host-side dispatch
 // --------------------------------------------------------------------------
-template <int KIND, int BN> struct B16Pick;   // operand stages OS
-template <> struct B16Pick<1, 128> { static constexpr int OS = 2; };
-template <> struct B16Pick<1, 256> { static constexpr int OS = 2; };
-template <> struct B16Pick<2, 128> { static constexpr int OS = 3; };
-template <> struct B16Pick<2, 256> { static constexpr int OS = 3; };
+template <int KIND, int BN> struct B16Pick;   // raw stages RS, operand stages OS
+template <> struct B16Pick<1, 128> { static constexpr int RS = 5, OS = 2; };
+template <> struct B16Pick<1, 256> { static constexpr int RS = 3, OS = 2; };
+template <> struct B16Pick<2, 128> { static constexpr int RS = 6, OS = 3; };
+template <> struct B16Pick<2, 256> { static constexpr int RS = 4, OS = 3; };
 
 #define MOE_B16_CASES(X) X(1, 128) X(1, 256) X(2, 128) X(2, 256)
 
@@ -413,8 +407,8 @@ template <int KIND, int BN>
 static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
                                   int grid, cudaStream_t st) {
   using P = B16Pick<KIND, BN>;
-  using C = B16Cfg<KIND, BN, P::OS>;
-  auto kern = moe_gemm_f16_kernel<KIND, BN, P::OS>;
+  using C = B16Cfg<KIND, BN, P::RS, P::OS>;
+  auto kern = moe_gemm_f16_kernel<KIND, BN, P::RS, P::OS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
@@ -422,7 +416,7 @@ static cudaError_t launch_f16_one(const CUtensorMap* tm_w, const CUtensorMap* tm
 
 size_t gemm_f16_partials_bytes(int kind, int bn, int grid) {
 #define X(KD, BB) \
-  if (kind == KD && bn == BB) return (size_t)grid * 2 * B16Cfg<KD, BB, 1>::NW * BB * 128 * sizeof(float);
+  if (kind == KD && bn == BB) return (size_t)grid * 2 * B16Cfg<KD, BB, 1, 1>::NW * BB * 128 * sizeof(float);
   MOE_B16_CASES(X)
 #undef X
   return 0;
