@@ -80,7 +80,7 @@ def measured_tensor_peak():
     return 1590.0, "fallback"
 
 
-WIDE_MIN_TOKENS = 2560      # the library switches to the f16-operand GEMMs here (api.cu)
+WIDE_MIN_TOKENS = 1536      # the library switches to the f16-operand GEMMs here (api.cu)
 
 
 def workload_name(T, E_l):

@@ -30,7 +30,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
 int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
-constexpr int kWideMinTokens = 2560;
+constexpr int kWideMinTokens = 1536;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -92,25 +92,22 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  // f16-operand GEMMs win once experts see ~80+ tokens each (measured on B200
-  // with 32 local experts: even at T=2048, 7% faster at 3072, 15% at 4096).
+  // f16-operand GEMMs win once experts see ~48+ tokens each (measured on B200
+  // with 32 local experts, layer time e4m3 / f16: T=1024 381/414 us, 1536
+  // 470/470, 2048 562/500, 3072 758/644, 16384 3047/2190).
   P->wide = g_path_override == 2 || (g_path_override == 0 && T >= kWideMinTokens);
   if (P->wide) {
     // f16 kernels accumulate in TMEM, so one tile takes up to 256 tokens.
-    // Wide tiles matter most: every weight byte a CTA converts then serves
-    // more tokens (measured on B200 at T=8192: GEMM1 with 128-token tiles
-    // 712 us, 112: 771, 80: 916).  The cap is also the token box height, so
-    // it follows the expected rows per expert (plus 30% for routing
-    // imbalance) where that is smaller.  GEMM1 tiles wider than 128 leave room
-    // for one TMEM accumulator only (X1 and X2), so its epilogue no longer
-    // overlaps the next tile; that pays only from ~384 rows per expert.
-    const double per_expert = 1.3 * (double)T * kTopK / kExpertsGlobal;
-    auto cap_for = [&](int widest) {
-      const int bn = ((int)ceil(per_expert) + 15) / 16 * 16;
-      return bn < 16 ? 16 : bn > widest ? widest : bn;
-    };
-    const int bn = cap_for(per_expert > 1.3 * 384.0 ? 256 : 128);
-    const int bn_2 = cap_for(256);
+    // The widest tiles win, measured on B200 with 32 local experts: each
+    // weight byte a CTA converts then serves the most tokens, and full-height
+    // token boxes (128 / 256 rows, loaded whether or not the tile fills them)
+    // stream faster than boxes cut to the expected rows (GEMM2 at T=4096:
+    // 228 us with 256-row boxes, 283 us with 176).  GEMM1 tiles wider than 128
+    // leave room for one TMEM accumulator only (X1 and X2), so its epilogue no
+    // longer overlaps the next tile; that pays only from ~384 rows per expert.
+    const double per_expert = (double)T * kTopK / kExpertsGlobal;
+    const int bn = per_expert > 384.0 ? 256 : 128;
+    const int bn_2 = 256;
     P->bn1 = g_bn_override[0] ? g_bn_override[0] : bn;
     P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_2;
     P->bt1 = P->bn1 > 128 ? 256 : 128;

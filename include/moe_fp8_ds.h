@@ -97,7 +97,7 @@ typedef struct moe_fp8_ds_layout {
   uint64_t down;            /* fp32  [R_cap, 7168] GEMM2 output per permuted row  */
   uint64_t act;             /* e4m3  [R_cap, 7168] permuted hidden rows (e4m3 GEMM1 input) */
   uint64_t act_scale;       /* fp32  [56, R_cap]  their 1x128 scales              */
-  /* The f16-operand GEMMs (T >= 2560) use these instead of act/act_scale/inter: */
+  /* The f16-operand GEMMs (T >= 1536) use these instead of act/act_scale/inter: */
   uint64_t act16;           /* f16   [R_cap, 7168] permuted rows, scales applied  */
   uint64_t inter16;         /* f16   [R_cap, 2048] SwiGLU output                  */
   int32_t row_capacity;     /* R_cap = T * min(8, E_l)                            */
@@ -168,7 +168,7 @@ MOE_API const char* moe_fp8_ds_status_string(int status);
 MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Tuning knob: 0 = automatic GEMM family (e4m3 block-promotion GEMMs for
- * T < 2560, f16-operand TMEM-accumulating GEMMs from 2560 tokens), 1 = always
+ * T < 1536, f16-operand TMEM-accumulating GEMMs from 1536 tokens), 1 = always
  * e4m3, 2 = always f16.  Takes effect for the next call (workspace size included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);
 

@@ -130,7 +130,7 @@ STAGE_CASES = [
     (300, 8, 0, 16, 0.0, (0, 0)),          # T > 256: 3-kernel front end, e4m3 GEMMs
     (300, 8, 0, 16, 0.0, (0, 0, 2)),       # f16-operand GEMMs forced at a small batch (64-token tiles)
     (4200, 8, 0, 17, 0.0, (0, 0, 1)),      # e4m3 GEMMs forced, 64/128-token tiles, many rows
-    (4200, 8, 0, 17, 0.0, (0, 0)),         # f16 GEMMs by default from 2560 tokens
+    (4200, 8, 0, 17, 0.0, (0, 0)),         # f16 GEMMs by default from 1536 tokens
     (4200, 8, 0, 17, 0.0, (96, 176, 2)),   # f16 GEMMs, tile caps below the compiled widths
     (4200, 8, 0, 17, 0.0, (208, 0, 2)),    # f16 GEMM1 with 256-token tiles (one TMEM accumulator)
     (2100, 8, 0, 18, 3.0, (0, 0, 2)),      # f16 GEMMs, skewed routing: hot experts with many tiles
@@ -142,7 +142,7 @@ def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
     inp = cached_inputs(T, E_l, off, seed, skew)
     path = bn[2] if len(bn) > 2 else 0
     out, ws, lay = run_layer(pkg, to_dev(inp, cuda_dev), bn=bn[:2], path=path)
-    wide = path == 2 or (path == 0 and T >= 2560)
+    wide = path == 2 or (path == 0 and T >= 1536)
     R = lay.row_capacity
     # routing
     ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
