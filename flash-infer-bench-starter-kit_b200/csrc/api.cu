@@ -77,7 +77,7 @@ struct Plan {
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
   int bt1, bt2;                     // compiled tile width of each GEMM (>= bn: the tile cap)
   bool wide;                        // large batch: f16-operand GEMMs (gemm_f16.cu)
-  uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2;
+  uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2, front_sync;
 };
 
 uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
@@ -141,6 +141,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->tiles1 = take((uint64_t)P->max_mt1 * 16);
   P->tiles2 = take((uint64_t)P->max_mt2 * 16);
   P->sched = take(64);
+  P->front_sync = take(16);
   P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->ready = take((uint64_t)E_l * 4);
@@ -284,13 +285,15 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   }
 
   cudaError_t ce;
-  if (!routed && T <= kFrontMaxTokens && !P.wide) {
+  const bool front = !routed && T <= kFrontMaxTokens && !P.wide;
+  if (front) {
     // Small batch: routing, row assignment and gather in one launch.
     mark_stage(0, s);
     ce = launch_front(a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
                       a->local_expert_offset, E_l, P.R_cap, P.bn1, P.bn2, kInter / 128, kHidden / 128,
                       a->hidden_states, a->hidden_states_scale, ids, wts, masks8, P.NB8, seg, tiles1, tiles2,
-                      sched, cnt1, cnt2, ready, inv, row_token, act, act_scale, err, s);
+                      sched, cnt1, cnt2, ready, inv, row_token, act, act_scale, err,
+                      reinterpret_cast<int*>(at(P.front_sync)), s);
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(1, s);
     mark_stage(2, s);
@@ -319,6 +322,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   mark_stage(3, s);
   g1.inter16 = inter16;
   g1.box_rows = P.bn1;
+  g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
+  g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
   ce = P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
               : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
@@ -337,7 +342,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
   mark_stage(5, s);
-  ce = launch_combine(down, inv, wts, T, a->output, a->output_f32, s);
+  ce = launch_combine(down, inv, wts, T, a->output, a->output_f32,
+                      front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr, err, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
   mark_stage(6, s);
   return MOE_OK;

@@ -114,10 +114,26 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) MOE_TL(0);
-  // GEMM1 waits for the routing/permutation kernels.  GEMM2 does not wait
-  // for GEMM1 as a whole: it starts streaming its weights on SMs GEMM1 has
-  // released and waits per expert (p.ready) before reading the intermediate.
-  if (KIND == 1 || !p.early_start) griddep_wait();
+  // GEMM1 waits for the routing/permutation kernels -- after the fused front
+  // kernel only for its tile lists (front_sync[0]), so the weight stream starts
+  // while the front kernel still gathers activations (front_sync[1] counts
+  // gathered CTAs; activations and their scales are read after it completes).
+  // GEMM2 does not wait for GEMM1 as a whole: it starts streaming its weights
+  // on SMs GEMM1 has released and waits per expert (p.ready) before reading
+  // the intermediate.
+  const bool early1 = KIND == 1 && p.front_sync != nullptr;
+  if (early1) {
+    __shared__ int s_front_ok;
+    if (threadIdx.x == 0) {
+      volatile int ab = 0;
+      s_front_ok = wait_counter(p.front_sync, 1, &ab) ? 1 : 0;
+      if (!s_front_ok) raise_error(p.err, kDevTimeoutBarrier);
+    }
+    __syncthreads();
+    if (!s_front_ok) return;   // uniform
+  } else if (KIND == 1 || !p.early_start) {
+    griddep_wait();
+  }
   if (threadIdx.x == 0) MOE_TL(1);
   griddep_launch_dependents();
   const WorkSched sch = make_work_sched(p.sched[KIND - 1], C::NT, C::KSTEPS);
@@ -145,6 +161,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       const uint64_t pol_b = l2_policy_evict_last();
       int issued = 0;
       int ready_e = -1;                 // GEMM2: expert whose intermediate is known complete
+      bool gathered = !early1;          // GEMM1 after the front kernel: activations written
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
         int u, ks, r;
@@ -166,6 +183,11 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           if (!wait_counter(p.ready + tile.x, target, abort_flag)) { ok = false; ++issued; break; }
           fence_proxy_async();
           ready_e = tile.x;
+        }
+        if (!gathered) {
+          if (!wait_counter(p.front_sync + 1, p.front_ctas, abort_flag)) { ok = false; ++issued; break; }
+          fence_proxy_async();
+          gathered = true;
         }
         tma_load_3d(&tm_b, &full[s], st + C::NW * KS * C::W_TILE, 0,
                     KIND == 1 ? tile.y : 2 * tile.y, z, pol_b);
@@ -245,6 +267,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
     const bool loader = et < C::SLOT;
     const int my_kk = et / (C::NW * BN), my_w = (et / BN) % C::NW, my_j = et % BN;
     int pf_unit = -1, pf_col = -1, pf_e = 0, pf_nt = 0;
+    bool pf_gathered = !early1;
     auto fetch = [&](int i_t) -> float {
       int u_t, ks_t, r_t;
       sch.at(i_t, C::KSTEPS, u_t, ks_t, r_t);
@@ -262,10 +285,14 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
       if (pf_col < 0) return 0.f;
+      if (!pf_gathered) {                               // act_scale is written by the front kernel
+        wait_counter(p.front_sync + 1, p.front_ctas, abort_flag);
+        pf_gathered = true;
+      }
       const int nb = KIND == 1 ? pf_nt + my_w * (kInter / 128) : pf_nt;
       const float wsc = __ldg(p.w_scale + ((size_t)pf_e * (C::W_ROWS / 128) + nb) * C::KB + kb_t);
       const float* bs = p.b_scale + (size_t)kb_t * p.R_cap + pf_col;
-      return wsc * ((KIND == 2 && p.early_start) ? __ldcg(bs) : __ldg(bs));
+      return wsc * (((KIND == 2 && p.early_start) || early1) ? __ldcg(bs) : __ldg(bs));
     };
     for (int i_t = 0; i_t < 2 && i_t < n_iter; ++i_t)
       if (loader) sring[i_t * C::SLOT + et] = fetch(i_t);

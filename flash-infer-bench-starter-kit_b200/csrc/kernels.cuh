@@ -16,6 +16,12 @@ struct GemmParams {
   const int32_t* seg;         // per-expert row offsets (GEMM2: rows of expert e)
   int bn_prev;                // GEMM2: GEMM1's token-tile width
   int box_rows;               // f16 GEMMs: rows of the token operand's TMA box (the tile cap)
+  // e4m3 GEMM1 after the fused front kernel: front_sync[0] = 1 once the tile
+  // lists are written, front_sync[1] counts front CTAs whose gather is done.
+  // GEMM1 starts streaming weights at the first and reads activations after
+  // the second reaches front_ctas (no grid-dependency wait).  nullptr: off.
+  int* front_sync;
+  int front_ctas;
   int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048]
@@ -113,10 +119,10 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
                          const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
                          int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
                          int32_t* counters1, int32_t* counters2, int* ready, int32_t* inv_row,
-                         int32_t* row_token, uint8_t* act, float* act_scale, int* err,
+                         int32_t* row_token, uint8_t* act, float* act_scale, int* err, int* front_sync,
                          cudaStream_t st);
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
-                           void* out, float* out_f32, cudaStream_t st);
+                           void* out, float* out_f32, const int* front_sync, int* err, cudaStream_t st);
 
 // Defined in api.cu: one full layer call on a caller-provided workspace.
 int run_layer_with_workspace(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream,

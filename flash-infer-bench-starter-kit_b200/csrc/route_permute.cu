@@ -451,7 +451,7 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
              int32_t* __restrict__ sched, int32_t* __restrict__ counters1,
              int32_t* __restrict__ counters2, int* __restrict__ ready, int32_t* __restrict__ inv_row,
              int32_t* __restrict__ row_token, uint8_t* __restrict__ act, float* __restrict__ act_scale,
-             int* __restrict__ err) {
+             int* __restrict__ err, int* __restrict__ front_sync) {
   __shared__ uint32_t s_mask[kExpertsGlobal];
   __shared__ int s_seg[kExpertsGlobal + 1];
   __shared__ int s_base[kExpertsGlobal];
@@ -464,7 +464,13 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   MOE_FTL(0);
   griddep_wait();
   MOE_FTL(1);
-  griddep_launch_dependents();
+  // GEMM1 is released only after the grid barrier below, so it cannot see the
+  // previous call's flags: they are cleared here, before CTA 0 reaches it.
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    front_sync[0] = 0;
+    front_sync[1] = 0;
+    __threadfence();
+  }
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
   if (threadIdx.x == 0) s_n = 0;
   __syncthreads();
@@ -482,6 +488,7 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   store_masks(masks8, NB8p, E_l, s_mask);
   MOE_FTL(2);
   if (!grid_barrier(err + 1, err + 2, err)) return;
+  griddep_launch_dependents();
   MOE_FTL(3);
   // ---- phase 2: per-expert counts and this CTA's first row per expert
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
@@ -531,6 +538,11 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     for (int i = threadIdx.x; i < units2; i += blockDim.x) counters2[i] = 0;
     for (int e = threadIdx.x; e < E_l; e += blockDim.x) ready[e] = 0;
     if (threadIdx.x == 0) { sched[0] = s_tot[1]; sched[1] = s_tot[2]; sched[2] = s_tot[0]; }
+    __syncthreads();
+    if (threadIdx.x == 0) {   // tile lists, schedule, counters published
+      __threadfence();
+      atomicExch(front_sync, 1);
+    }
   }
   MOE_FTL(4);
   // ---- phase 3: rows of own tokens, inverse map, activation gather
@@ -578,6 +590,10 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
   }
   __syncthreads();
+  if (threadIdx.x == 0) {     // this CTA's rows of act / act_scale are written
+    __threadfence();
+    atomicAdd(front_sync + 1, 1);
+  }
   MOE_FTL(5);
 }
 
@@ -588,15 +604,25 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
 __global__ void __launch_bounds__(256)
 combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_row,
                const float* __restrict__ topk_w, int T, __nv_bfloat16* __restrict__ out,
-               float* __restrict__ out_f32) {
+               float* __restrict__ out_f32, const int* __restrict__ front_sync, int front_ctas,
+               int* __restrict__ err) {
   griddep_wait();
   griddep_launch_dependents();
   const int t = blockIdx.x;
   __shared__ int s_row[kTopK];
   __shared__ float s_w[kTopK];
+  // After the fused front kernel the GEMMs do not wait for its completion, so
+  // when no GEMM work depended on it (no local rows) the grid dependency does
+  // not cover it either: wait for its gather count (bounded) before reading
+  // the routing and row map it wrote.
+  if (front_sync != nullptr && threadIdx.x == 0) {
+    volatile int ab = 0;
+    if (!wait_counter(front_sync + 1, front_ctas, &ab)) raise_error(err, kDevTimeoutBarrier);
+  }
+  __syncthreads();
   if (threadIdx.x < kTopK) {
-    s_row[threadIdx.x] = inv_row[(size_t)t * kTopK + threadIdx.x];
-    s_w[threadIdx.x] = topk_w[(size_t)t * kTopK + threadIdx.x];
+    s_row[threadIdx.x] = __ldcg(inv_row + (size_t)t * kTopK + threadIdx.x);
+    s_w[threadIdx.x] = __ldcg(topk_w + (size_t)t * kTopK + threadIdx.x);
   }
   __syncthreads();
   for (int v = blockIdx.y * blockDim.x + threadIdx.x; v < kHidden / 4; v += blockDim.x * gridDim.y) {
@@ -666,21 +692,23 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
                          const float* hs_scale, int32_t* ids, float* w, uint8_t* masks8, int NB8p,
                          int32_t* seg, int4* tiles1, int4* tiles2, int32_t* sched,
                          int32_t* counters1, int32_t* counters2, int* ready, int32_t* inv_row,
-                         int32_t* row_token, uint8_t* act, float* act_scale, int* err,
+                         int32_t* row_token, uint8_t* act, float* act_scale, int* err, int* front_sync,
                          cudaStream_t st) {
   const int nb = (T + kRouteTokens - 1) / kRouteTokens;
   if (nb == 0) return cudaSuccess;
   return launch_pdl(front_kernel, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits,
                     static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, R_cap, bn1,
                     bn2, nt1, nt2, static_cast<const uint8_t*>(hidden), hs_scale, ids, w, masks8, NB8p, seg,
-                    tiles1, tiles2, sched, counters1, counters2, ready, inv_row, row_token, act, act_scale, err);
+                    tiles1, tiles2, sched, counters1, counters2, ready, inv_row, row_token, act, act_scale, err,
+                    front_sync);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
-                           void* out, float* out_f32, cudaStream_t st) {
+                           void* out, float* out_f32, const int* front_sync, int* err, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
+  const int front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
   return launch_pdl(combine_kernel, dim3(T, (kHidden / 4 + 255) / 256), dim3(256), 0, st, down, inv_row, w, T,
-                    static_cast<__nv_bfloat16*>(out), out_f32);
+                    static_cast<__nv_bfloat16*>(out), out_f32, front_sync, front_ctas, err);
 }
 
 }  // namespace moe

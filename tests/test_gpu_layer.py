@@ -257,3 +257,18 @@ def test_rejects_bad_arguments(pkg, cuda_dev):
     bad["gemm2_weights_scale"] = inp["gemm2_weights_scale"][:, :55]
     with pytest.raises(ValueError):
         pkg.kernel(*pkg.inputs.as_args(bad), torch.empty(1, 7168, dtype=torch.bfloat16, device=cuda_dev))
+
+
+def test_no_local_rows_zero_output(pkg, oracle, cuda_dev):
+    """A batch none of whose tokens picks a local expert: the GEMMs get no
+    work, so the combine must still wait for the front kernel's row map and
+    write an all-zero output (twice in a row, reusing the workspace)."""
+    inp = cached_inputs(48, 1, 0, 19)
+    ids, _, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    unused = sorted(set(range(256)) - set(ids.flatten().tolist()))
+    assert unused, "every expert was picked; pick another seed"
+    d = to_dev(dict(inp, local_expert_offset=unused[0]), cuda_dev)
+    out, ws, _ = run_layer(pkg, d)
+    assert torch.count_nonzero(out.float()) == 0
+    out2, _, _ = run_layer(pkg, d, ws=ws)
+    assert torch.count_nonzero(out2.float()) == 0
