@@ -42,19 +42,20 @@ struct GemmParams {
 //            is finished by its last contributor (fixed-order reduction).
 struct WorkSched {
   int n_mt, units, Wf, n1, it0, it1, L;
+  int G, gid;                 // workers (CTAs, or CTA pairs) and this worker's index
   __device__ __forceinline__ int n_iter() const { return n1 + it1 - it0; }
   // Local iteration i -> unit u, iteration a inside the unit, and the unit's
   // phase-2 index r (-1 in phase 1: never split).
   __device__ __forceinline__ void at(int i, int ITERS, int& u, int& a, int& r) const {
     if (i < n1) {
-      u = (i / ITERS) * (int)gridDim.x + (int)blockIdx.x;
+      u = (i / ITERS) * G + gid;
       a = i % ITERS;
       r = -1;
     } else {
       const int it = it0 + i - n1;
       r = it / ITERS;
       a = it % ITERS;
-      u = Wf * (int)gridDim.x + r;
+      u = Wf * G + r;
     }
   }
   __device__ __forceinline__ int unit_of(int i, int ITERS) const {
@@ -62,28 +63,33 @@ struct WorkSched {
     at(i, ITERS, u, a, r);
     return u;
   }
-  // First CTA and last CTA contributing to phase-2 unit r.
+  // First and last worker contributing to phase-2 unit r.
   __device__ __forceinline__ int first_cta(int r, int ITERS) const { return (r * ITERS) / L; }
   __device__ __forceinline__ int last_cta(int r, int ITERS) const { return ((r + 1) * ITERS - 1) / L; }
-  // Partial-tile slot CTA c uses for phase-2 unit r: 0 for the unit its range
-  // starts in, 1 for the one it ends in.
+  // Partial-tile slot worker c uses for phase-2 unit r: 0 for the unit its
+  // range starts in, 1 for the one it ends in.
   __device__ __forceinline__ int slot(int c, int r, int ITERS) const {
     return r == (c * L) / ITERS ? 0 : 1;
   }
 };
 
-__device__ __forceinline__ WorkSched make_work_sched(int n_mt, int NT, int ITERS) {
+__device__ __forceinline__ WorkSched make_work_sched_for(int n_mt, int NT, int ITERS, int G, int gid) {
   WorkSched s;
-  const int G = gridDim.x;
+  s.G = G;
+  s.gid = gid;
   s.n_mt = n_mt;
   s.units = n_mt * NT;
   s.Wf = s.units / G;
   s.n1 = s.Wf * ITERS;
   const int total2 = (s.units - s.Wf * G) * ITERS;
   s.L = max(1, (total2 + G - 1) / G);
-  s.it0 = min(total2, (int)blockIdx.x * s.L);
+  s.it0 = min(total2, gid * s.L);
   s.it1 = min(total2, s.it0 + s.L);
   return s;
+}
+
+__device__ __forceinline__ WorkSched make_work_sched(int n_mt, int NT, int ITERS) {
+  return make_work_sched_for(n_mt, NT, ITERS, (int)gridDim.x, (int)blockIdx.x);
 }
 
 // Token-tile configurations compiled for each GEMM (BN = tokens per tile).
@@ -96,6 +102,13 @@ int gemm_k_per_stage(int kind, int bn);
 int gemm_ctas_per_sm(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st);
+
+// f16-operand GEMMs on CTA pairs (gemm_f16_pair.cu): 0 from gemm_pair_grid
+// means clusters of two cannot be resident.
+int gemm_pair_grid(int kind, int sm_count);
+size_t gemm_pair_partials_bytes(int grid);
+cudaError_t launch_gemm_pair(int kind, const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
+                             int grid, cudaStream_t st);
 
 // f16-operand GEMMs for large batches (gemm_f16.cu).
 size_t gemm_f16_partials_bytes(int kind, int bn, int grid);
