@@ -143,11 +143,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
   uint64_t* accf = opempty + OS;                            // accumulator b complete
   uint64_t* acce = accf + 2;                                // accumulator b drained
   uint64_t* drain = acce + 2;
-#ifdef MOE_F16_EXTRA_COMMITS
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 2);   // drain + 1: dummy barrier
-#else
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
-#endif
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = const_cast<int*>(abort_flag) + 1;
 
@@ -165,9 +161,6 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
     for (int o = 0; o < OS; ++o) { mbar_init(&conv[o], C::NCONV); mbar_init(&opempty[o], 1); }
     for (int b = 0; b < 2; ++b) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
     mbar_init(drain, 1);
-#ifdef MOE_F16_EXTRA_COMMITS
-    mbar_init(drain + 1, 1);
-#endif
     *const_cast<int*>(abort_flag) = 0;
     fence_mbar_init();
   }
@@ -250,9 +243,6 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         }
         tc_commit(&empty[s]);
         tc_commit(&opempty[o]);
-#ifdef MOE_F16_EXTRA_COMMITS
-        for (int xc = 0; xc < MOE_F16_EXTRA_COMMITS; ++xc) tc_commit(drain + 1);   // diagnostics: commit cost (dummy barrier)
-#endif
         if (seg_last) { tc_commit(&accf[b]); ++seg; }
       }
       if (!ok) raise_error(p.err, kDevTimeoutMma);
