@@ -601,7 +601,15 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
 // Combine: out[t] = sum_k w[t,k] * down[inv[t,k]] over local picks, in
 // ascending expert order, fp32 multiply-then-add (as index_add_ does), then bf16.
 // --------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
+constexpr int kCombineThreads = 224;                        // 1792 float4 per row = 224 x 8
+constexpr int kCombineRowVec = kHidden / 4 / kCombineThreads;
+static_assert(kCombineRowVec * kCombineThreads * 4 == kHidden, "combine row split");
+
+// VEC float4 columns per thread: a CTA covers VEC/8 of a token row
+// (gridDim.y = 8 / VEC).  Large batches use whole rows per CTA (fewer, fuller
+// CTAs, 8 loads in flight per thread); small ones split rows for parallelism.
+template <int VEC>
+__global__ void __launch_bounds__(kCombineThreads)
 combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_row,
                const float* __restrict__ topk_w, int T, __nv_bfloat16* __restrict__ out,
                float* __restrict__ out_f32, const int* __restrict__ front_sync, int front_ctas,
@@ -620,29 +628,49 @@ combine_kernel(const float* __restrict__ down, const int32_t* __restrict__ inv_r
     if (!wait_counter(front_sync + 1, front_ctas, &ab)) raise_error(err, kDevTimeoutBarrier);
   }
   __syncthreads();
-  if (threadIdx.x < kTopK) {
-    s_row[threadIdx.x] = __ldcg(inv_row + (size_t)t * kTopK + threadIdx.x);
-    s_w[threadIdx.x] = __ldcg(topk_w + (size_t)t * kTopK + threadIdx.x);
+  __shared__ int s_n;
+  if (threadIdx.x < 32) {   // this token's local picks, compacted in ascending k
+    const int k = threadIdx.x;
+    const int r = k < kTopK ? __ldcg(inv_row + (size_t)t * kTopK + k) : -1;
+    const float wk = k < kTopK ? __ldcg(topk_w + (size_t)t * kTopK + k) : 0.f;
+    const uint32_t m = __ballot_sync(0xffffffffu, r >= 0);
+    if (r >= 0) {
+      const int pos = __popc(m & ((1u << k) - 1u));
+      s_row[pos] = r;
+      s_w[pos] = wk;
+    }
+    if (k == 0) s_n = __popc(m);
   }
   __syncthreads();
-  for (int v = blockIdx.y * blockDim.x + threadIdx.x; v < kHidden / 4; v += blockDim.x * gridDim.y) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Each thread owns VEC float4 columns and issues all of a pick's loads
+  // before adding them (fp32 multiply-then-add in ascending k, as index_add_).
+  const int n = s_n;
+  const int v0 = blockIdx.y * VEC * kCombineThreads + threadIdx.x;
+  float4 acc[VEC];
 #pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
-      const int r = s_row[k];
-      if (r < 0) continue;
-      const float w = s_w[k];
-      float4 o = __ldcs(reinterpret_cast<const float4*>(down + (size_t)r * kHidden) + v);
-      acc.x = __fadd_rn(acc.x, __fmul_rn(o.x, w));
-      acc.y = __fadd_rn(acc.y, __fmul_rn(o.y, w));
-      acc.z = __fadd_rn(acc.z, __fmul_rn(o.z, w));
-      acc.w = __fadd_rn(acc.w, __fmul_rn(o.w, w));
+  for (int c = 0; c < VEC; ++c) acc[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int k = 0; k < n; ++k) {
+    const float w = s_w[k];
+    const float4* src = reinterpret_cast<const float4*>(down + (size_t)s_row[k] * kHidden);
+    float4 o[VEC];
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) o[c] = __ldcs(src + v0 + c * kCombineThreads);
+#pragma unroll
+    for (int c = 0; c < VEC; ++c) {
+      acc[c].x = __fadd_rn(acc[c].x, __fmul_rn(o[c].x, w));
+      acc[c].y = __fadd_rn(acc[c].y, __fmul_rn(o[c].y, w));
+      acc[c].z = __fadd_rn(acc[c].z, __fmul_rn(o[c].z, w));
+      acc[c].w = __fadd_rn(acc[c].w, __fmul_rn(o[c].w, w));
     }
+  }
+#pragma unroll
+  for (int c = 0; c < VEC; ++c) {
+    const int v = v0 + c * kCombineThreads;
     if (out_f32) {
-      reinterpret_cast<float4*>(out_f32 + (size_t)t * kHidden)[v] = acc;
+      reinterpret_cast<float4*>(out_f32 + (size_t)t * kHidden)[v] = acc[c];
     } else {
-      __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+      __nv_bfloat162 lo = __floats2bfloat162_rn(acc[c].x, acc[c].y);
+      __nv_bfloat162 hi = __floats2bfloat162_rn(acc[c].z, acc[c].w);
       uint2 packed;
       packed.x = *reinterpret_cast<uint32_t*>(&lo);
       packed.y = *reinterpret_cast<uint32_t*>(&hi);
@@ -707,8 +735,11 @@ cudaError_t launch_combine(const float* down, const int32_t* inv_row, const floa
                            void* out, float* out_f32, const int* front_sync, int* err, cudaStream_t st) {
   if (T == 0) return cudaSuccess;
   const int front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
-  return launch_pdl(combine_kernel, dim3(T, (kHidden / 4 + 255) / 256), dim3(256), 0, st, down, inv_row, w, T,
-                    static_cast<__nv_bfloat16*>(out), out_f32, front_sync, front_ctas, err);
+  if (T >= 512)
+    return launch_pdl(combine_kernel<kCombineRowVec>, dim3(T, 1), dim3(kCombineThreads), 0, st, down, inv_row,
+                      w, T, static_cast<__nv_bfloat16*>(out), out_f32, front_sync, front_ctas, err);
+  return launch_pdl(combine_kernel<1>, dim3(T, kCombineRowVec), dim3(kCombineThreads), 0, st, down, inv_row, w,
+                    T, static_cast<__nv_bfloat16*>(out), out_f32, front_sync, front_ctas, err);
 }
 
 }  // namespace moe
