@@ -368,29 +368,54 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
     }
   }
   s_row[threadIdx.x] = row;
+  // local (row, token) pairs, compacted (their order does not matter)
+  __shared__ int2 s_list[kPermBlock * kTopK];
+  __shared__ int s_n;
+  if (threadIdx.x == 0) s_n = 0;
   __syncthreads();
-  // copy: 16-byte vectors, (pair, vector) flattened over the CTA.  With act16
-  // the rows are written in f16 with their 1x128 scales applied (operand of
-  // the f16 GEMMs); otherwise as e4m3 plus the scales.
+  {
+    const uint32_t m = __ballot_sync(0xffffffffu, row >= 0);
+    int base = 0;
+    if ((threadIdx.x & 31) == 0 && m) base = atomicAdd(&s_n, __popc(m));
+    base = __shfl_sync(0xffffffffu, base, 0);
+    if (row >= 0) s_list[base + __popc(m & ((1u << (threadIdx.x & 31)) - 1u))] = make_int2(row, t);
+  }
+  __syncthreads();
+  // copy: 16-byte vectors of the compacted pairs, kBatch loads in flight per
+  // thread before the stores.  With act16 the rows are written in f16 with
+  // their 1x128 scales applied (operand of the f16 GEMMs); otherwise as e4m3
+  // plus the scales.
   constexpr int kVec = kGatherChunk / 16;
+  constexpr int kBatch = 4;
   const size_t col = (size_t)blockIdx.y * kGatherChunk;
-  for (int v = threadIdx.x; v < kPermBlock * kTopK * kVec; v += blockDim.x) {
-    const int pr = v / kVec;
-    const int r = s_row[pr];
-    if (r < 0) continue;
-    const int tok = blockIdx.x * kPermBlock + pr / kTopK;
-    const int off = (v % kVec) * 16;
-    const uint4 val = __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)tok * kHidden + col + off));
-    if (act16) {
-      const int kb = (int)((col + off) / kBlock);
-      const float sc = __ldg(hs_scale + (size_t)kb * T + tok);
-      uint4 lo, hi;
-      e4m3x16_to_f16(val, sc, lo, hi);
-      uint4* dst = reinterpret_cast<uint4*>(act16 + (size_t)r * kHidden + col + off);
-      dst[0] = lo;
-      dst[1] = hi;
-    } else {
-      *reinterpret_cast<uint4*>(act + (size_t)r * kHidden + col + off) = val;
+  const int nvec = s_n * kVec;
+  for (int v0 = threadIdx.x; v0 < nvec; v0 += kBatch * blockDim.x) {
+    uint4 val[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      if (v < nvec) {
+        const int2 rt = s_list[v / kVec];
+        val[u] = __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)rt.y * kHidden + col + (v % kVec) * 16));
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int v = v0 + u * blockDim.x;
+      if (v >= nvec) break;
+      const int2 rt = s_list[v / kVec];
+      const int off = (v % kVec) * 16;
+      if (act16) {
+        const int kb = (int)((col + off) / kBlock);
+        const float sc = __ldg(hs_scale + (size_t)kb * T + rt.y);
+        uint4 lo, hi;
+        e4m3x16_to_f16(val[u], sc, lo, hi);
+        uint4* dst = reinterpret_cast<uint4*>(act16 + (size_t)rt.x * kHidden + col + off);
+        dst[0] = lo;
+        dst[1] = hi;
+      } else {
+        *reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden + col + off) = val[u];
+      }
     }
   }
   if (!act16) {
