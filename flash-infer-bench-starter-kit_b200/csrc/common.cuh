@@ -173,16 +173,6 @@ __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
-// 2D tiled load global -> shared, completion counted on an mbarrier (no multicast).
-__device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
-                                            int32_t x, int32_t y, uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
-      : "memory");
-}
-
 // 3D tiled load: x = byte inside a 128-byte K block, y = row, z = K block.
 __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
                                             int32_t x, int32_t y, int32_t z, uint64_t policy) {
@@ -203,20 +193,6 @@ __device__ __forceinline__ uint64_t l2_policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
   return p;
-}
-
-// 2D gather of four rows (tile::gather4): x = first column, rows r0..r3;
-// the tensor map's box is 128 columns x 1 row and the four rows land as
-// consecutive 128-byte rows at smem_dst.
-__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
-                                            int32_t x, int32_t r0, int32_t r1, int32_t r2, int32_t r3,
-                                            uint64_t policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1), "r"(r2),
-      "r"(r3), "l"(policy)
-      : "memory");
 }
 
 // ---- tcgen05 / TMEM -------------------------------------------------------

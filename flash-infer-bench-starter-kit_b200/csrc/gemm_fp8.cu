@@ -545,14 +545,6 @@ int gemm_ctas_per_sm(int kind, int bn) {
   return 1;
 }
 
-int gemm_threads(int kind, int bn) {
-#define X(KD, BB) \
-  if (kind == KD && bn == BB) return CfgOf<KD, BB>::THREADS;
-  MOE_GEMM_CASES(X)
-#undef X
-  return 0;
-}
-
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st) {
 #define X(KD, BB) \

@@ -92,12 +92,7 @@ __device__ __forceinline__ WorkSched make_work_sched(int n_mt, int NT, int ITERS
   return make_work_sched_for(n_mt, NT, ITERS, (int)gridDim.x, (int)blockIdx.x);
 }
 
-// Token-tile configurations compiled for each GEMM (BN = tokens per tile).
-constexpr int kNumBnConfigs = 4;
-constexpr int kBnConfigs[kNumBnConfigs] = {16, 32, 64, 128};
-
 size_t gemm_partials_bytes(int kind, int bn, int grid);
-int gemm_threads(int kind, int bn);
 int gemm_k_per_stage(int kind, int bn);
 int gemm_ctas_per_sm(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,

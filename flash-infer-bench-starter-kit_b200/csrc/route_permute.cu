@@ -58,11 +58,7 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
     float s[8], sb[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-#ifdef MOE_ROUTE_EXPF_PROBE
-      float e = expf(-x[j]);
-#else
       float e = (float)exp(-(double)x[j]);
-#endif
       s[j] = __frcp_rn(__fadd_rn(1.0f, e));
       sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
     }
