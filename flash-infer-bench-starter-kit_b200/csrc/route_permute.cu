@@ -62,6 +62,7 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
       s[j] = __frcp_rn(__fadd_rn(1.0f, e));
       sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
     }
+    MOE_FTL(6);
     // ---- group score: sum of the top-2 sb of each 32-expert group
     float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
@@ -92,32 +93,46 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
       keep |= 1u << best;
     }
     const bool my_group_kept = (keep >> (lane >> 2)) & 1u;
-    // ---- top-8 experts of sb inside kept groups
+    // ---- top-8 experts of sb inside kept groups.  Each lane keeps the index
+    // of its best untaken candidate (lowest j on ties); a round takes the
+    // warp-wide maximum with one redux on an order-preserving integer key,
+    // and the lowest lane holding it (= lowest expert id on ties) gives it up.
+    auto key_of = [](float v) -> uint32_t {   // monotone float -> u32
+      const uint32_t b = __float_as_uint(v);
+      return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+    };
     float cand[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) cand[j] = my_group_kept ? sb[j] : -INFINITY;
     unsigned taken = 0;
-    int sel_e[kTopK];
-    float sel_s[kTopK];
-#pragma unroll
-    for (int k = 0; k < kTopK; ++k) {
+    auto local_best = [&]() -> int {
       int bj = -1; float bv = -INFINITY;
 #pragma unroll
       for (int j = 0; j < 8; ++j)
         if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) { bj = j; bv = cand[j]; }
-      int be = lane * 8 + bj;
+      return bj;
+    };
+    int bj = local_best();
+    int sel_e[kTopK];
+    float sel_s[kTopK];
 #pragma unroll
-      for (int off = 16; off >= 1; off >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-        int oe = __shfl_xor_sync(0xffffffffu, be, off);
-        if (ov > bv || (ov == bv && oe < be)) { bv = ov; be = oe; }
+    for (int k = 0; k < kTopK; ++k) {
+      float bv = -INFINITY, bs = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) if (j == bj) { bv = cand[j]; bs = s[j]; }
+      const uint32_t key = bj < 0 ? 0u : key_of(bv);
+      const uint32_t top = __reduce_max_sync(0xffffffffu, key);
+      const uint32_t holders = __ballot_sync(0xffffffffu, key == top);
+      const int wl = __ffs(holders) - 1;
+      const int wj = __shfl_sync(0xffffffffu, bj, wl);
+      sel_e[k] = wl * 8 + wj;
+      sel_s[k] = __shfl_sync(0xffffffffu, bs, wl);
+      if (lane == wl) {
+        taken |= 1u << wj;
+        bj = local_best();
       }
-      float my_s = 0.f;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) if (be == lane * 8 + j) { taken |= 1u << j; my_s = s[j]; }
-      sel_e[k] = be;
-      sel_s[k] = __shfl_sync(0xffffffffu, my_s, be >> 3);
     }
+    MOE_FTL(7);
     // ---- sort the 8 picks ascending (all lanes hold the same arrays)
 #pragma unroll
     for (int a = 1; a < kTopK; ++a)
