@@ -468,7 +468,7 @@ __device__ bool grid_barrier(int* count, volatile int* gen, int* err) {
       const unsigned long long t0 = globaltimer_ns();
       while (*gen == g) {
         if (globaltimer_ns() - t0 > kWaitLimitNs) { ok = 0; raise_error(err, kDevTimeoutBarrier); break; }
-        __nanosleep(64);
+        // spin: the waiting is short and its latency is on the critical path
       }
     }
     __threadfence();
@@ -523,7 +523,18 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   __syncthreads();
   store_masks(masks8, NB8p, E_l, s_mask);
   MOE_FTL(2);
-  if (!grid_barrier(err + 1, err + 2, err)) return;
+  // Up to eight CTAs run as one thread-block cluster (launch attribute) and
+  // meet at the hardware cluster barrier, which also orders their global
+  // writes (release/acquire at cluster scope); larger grids use the bounded
+  // software grid barrier.
+  uint32_t nctas_in_cluster;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(nctas_in_cluster));
+  if (nctas_in_cluster == gridDim.x && gridDim.x > 1) {
+    __syncthreads();
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  } else if (!grid_barrier(err + 1, err + 2, err)) {
+    return;
+  }
   griddep_launch_dependents();
   MOE_FTL(3);
   // ---- phase 2: per-expert counts and this CTA's first row per expert
@@ -760,11 +771,27 @@ cudaError_t launch_front(const float* logits, const void* bias, int T, float sca
                          cudaStream_t st) {
   const int nb = (T + kRouteTokens - 1) / kRouteTokens;
   if (nb == 0) return cudaSuccess;
-  return launch_pdl(front_kernel, dim3(nb), dim3(kRouteTokens * 32), 0, st, logits,
-                    static_cast<const __nv_bfloat16*>(bias), T, scaling, local_offset, E_l, R_cap, bn1,
-                    bn2, nt1, nt2, static_cast<const uint8_t*>(hidden), hs_scale, ids, w, masks8, NB8p, seg,
-                    tiles1, tiles2, sched, counters1, counters2, ready, inv_row, row_token, act, act_scale, err,
-                    front_sync);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(nb);
+  cfg.blockDim = dim3(kRouteTokens * 32);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  int na = 1;
+  if (nb > 1 && nb <= 8) {   // one cluster: hardware barrier instead of global atomics
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = nb;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    na = 2;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  return cudaLaunchKernelEx(&cfg, front_kernel, logits, static_cast<const __nv_bfloat16*>(bias), T, scaling,
+                            local_offset, E_l, R_cap, bn1, bn2, nt1, nt2, static_cast<const uint8_t*>(hidden),
+                            hs_scale, ids, w, masks8, NB8p, seg, tiles1, tiles2, sched, counters1, counters2, ready,
+                            inv_row, row_token, act, act_scale, err, front_sync);
 }
 
 cudaError_t launch_combine(const float* down, const int32_t* inv_row, const float* w, int T,
