@@ -1,4 +1,4 @@
-// Grouped GEMMs for large batches (T > 256 tokens): block scales folded into
+// Grouped GEMMs for large batches (from 1536 tokens by default): block scales folded into
 // f16 operands, whole-K accumulation in TMEM.
 //
 // The e4m3 GEMMs (gemm_fp8.cu) must promote every 128-wide K block from TMEM
