@@ -496,12 +496,24 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 // Host-side dispatch: (kind, BN) -> stages, warpgroups, K blocks per stage.
 // --------------------------------------------------------------------------
 template <int KIND, int BN> struct Pick;
-template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
+#ifndef MOE_P116_S
+#define MOE_P116_S 3
+#define MOE_P116_K 2
+#endif
+#ifndef MOE_P216_S
+#define MOE_P216_S 2   // four K blocks per stage: 64 KB weight boxes (T=64: GEMM2 58 -> 51 us)
+#define MOE_P216_K 4
+#endif
+#ifndef MOE_P232_S
+#define MOE_P232_S 2   // likewise for 32-token tiles (T=600: GEMM2 124 -> 98 us)
+#define MOE_P232_K 4
+#endif
+template <> struct Pick<1, 16> { static constexpr int S = MOE_P116_S, W = 1, K = MOE_P116_K, O = 1; };
 template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<1, 64> { static constexpr int S = 2, W = 2, K = 2, O = 1; };
 template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
-template <> struct Pick<2, 16> { static constexpr int S = 5, W = 1, K = 2, O = 1; };
-template <> struct Pick<2, 32> { static constexpr int S = 4, W = 1, K = 2, O = 1; };
+template <> struct Pick<2, 16> { static constexpr int S = MOE_P216_S, W = 1, K = MOE_P216_K, O = 1; };
+template <> struct Pick<2, 32> { static constexpr int S = MOE_P232_S, W = 1, K = MOE_P232_K, O = 1; };
 template <> struct Pick<2, 64> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
 
