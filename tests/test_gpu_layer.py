@@ -125,6 +125,7 @@ STAGE_CASES = [
     (64, 32, 0, 13, 0.0, (0, 0)),
     (200, 8, 0, 14, 3.0, (16, 16)),
     (200, 8, 0, 14, 3.0, (32, 64)),
+    (200, 8, 0, 14, 3.0, (16, 32)),        # 32-token GEMM2 tiles (four K blocks per stage)
     (200, 8, 0, 14, 3.0, (128, 128)),
     (130, 16, 16, 15, 0.0, (64, 32)),
     (300, 8, 0, 16, 0.0, (0, 0)),          # T > 256: 3-kernel front end, e4m3 GEMMs
