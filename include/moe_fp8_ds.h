@@ -169,7 +169,9 @@ MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Tuning knob: 0 = automatic GEMM family (e4m3 block-promotion GEMMs for
  * T < 1536, f16-operand TMEM-accumulating GEMMs from 1536 tokens), 1 = always
- * e4m3, 2 = always f16, 3 = always f16 on CTA pairs (cta_group::2, M = 256).  Takes effect for the next call (workspace size included). */
+ * e4m3, 2 = always f16, 3 = always f16 on CTA pairs (cta_group::2, M = 256;
+ * correct but measured slower, never chosen automatically).  Takes effect for
+ * the next call (workspace size included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);
 
 /* Profiling hook: when `count` is 7, later calls on this process record
