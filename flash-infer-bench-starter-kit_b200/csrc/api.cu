@@ -112,9 +112,11 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
     // stream faster than boxes cut to the expected rows (GEMM2 at T=4096:
     // 228 us with 256-row boxes, 283 us with 176).  GEMM1 tiles wider than 128
     // leave room for one TMEM accumulator only (X1 and X2), so its epilogue no
-    // longer overlaps the next tile; that pays only from ~384 rows per expert.
+    // longer overlaps the next tile; that pays only from ~384 rows per expert
+    // (GEMM1 256 / 128-token tiles, layer us: T=4096 743/618, 8192 941/914,
+    // 12288 1253/1270).
     const double per_expert = (double)T * kTopK / kExpertsGlobal;
-    const int bn = per_expert > 384.0 ? 256 : 128;
+    const int bn = per_expert >= 384.0 ? 256 : 128;
     const int bn_2 = 256;
     P->bn1 = g_bn_override[0] ? g_bn_override[0] : bn;
     P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_2;
