@@ -91,7 +91,7 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 // their weight tiles, so the two or three token tiles of one expert read each
 // weight tile from L2 rather than from HBM again, and each expert's tiles finish
 // together (the early-start consumer waits per expert).
-__device__ __forceinline__ int2 unit_tile(int u, int n_mt, int NT) {
+__host__ __device__ __forceinline__ int2 unit_tile(int u, int n_mt, int NT) {
 #ifdef MOE_UNIT_NT_MAJOR
   return make_int2(u % n_mt, u / n_mt);
 #else

@@ -43,10 +43,10 @@ struct GemmParams {
 struct WorkSched {
   int n_mt, units, Wf, n1, it0, it1, L;
   int G, gid;                 // workers (CTAs, or CTA pairs) and this worker's index
-  __device__ __forceinline__ int n_iter() const { return n1 + it1 - it0; }
+  __host__ __device__ __forceinline__ int n_iter() const { return n1 + it1 - it0; }
   // Local iteration i -> unit u, iteration a inside the unit, and the unit's
   // phase-2 index r (-1 in phase 1: never split).
-  __device__ __forceinline__ void at(int i, int ITERS, int& u, int& a, int& r) const {
+  __host__ __device__ __forceinline__ void at(int i, int ITERS, int& u, int& a, int& r) const {
     if (i < n1) {
       u = (i / ITERS) * G + gid;
       a = i % ITERS;
@@ -58,22 +58,22 @@ struct WorkSched {
       u = Wf * G + r;
     }
   }
-  __device__ __forceinline__ int unit_of(int i, int ITERS) const {
+  __host__ __device__ __forceinline__ int unit_of(int i, int ITERS) const {
     int u, a, r;
     at(i, ITERS, u, a, r);
     return u;
   }
   // First and last worker contributing to phase-2 unit r.
-  __device__ __forceinline__ int first_cta(int r, int ITERS) const { return (r * ITERS) / L; }
-  __device__ __forceinline__ int last_cta(int r, int ITERS) const { return ((r + 1) * ITERS - 1) / L; }
+  __host__ __device__ __forceinline__ int first_cta(int r, int ITERS) const { return (r * ITERS) / L; }
+  __host__ __device__ __forceinline__ int last_cta(int r, int ITERS) const { return ((r + 1) * ITERS - 1) / L; }
   // Partial-tile slot worker c uses for phase-2 unit r: 0 for the unit its
   // range starts in, 1 for the one it ends in.
-  __device__ __forceinline__ int slot(int c, int r, int ITERS) const {
+  __host__ __device__ __forceinline__ int slot(int c, int r, int ITERS) const {
     return r == (c * L) / ITERS ? 0 : 1;
   }
 };
 
-__device__ __forceinline__ WorkSched make_work_sched_for(int n_mt, int NT, int ITERS, int G, int gid) {
+__host__ __device__ __forceinline__ WorkSched make_work_sched_for(int n_mt, int NT, int ITERS, int G, int gid) {
   WorkSched s;
   s.G = G;
   s.gid = gid;
@@ -82,9 +82,9 @@ __device__ __forceinline__ WorkSched make_work_sched_for(int n_mt, int NT, int I
   s.Wf = s.units / G;
   s.n1 = s.Wf * ITERS;
   const int total2 = (s.units - s.Wf * G) * ITERS;
-  s.L = max(1, (total2 + G - 1) / G);
-  s.it0 = min(total2, gid * s.L);
-  s.it1 = min(total2, s.it0 + s.L);
+  s.L = (total2 + G - 1) / G > 1 ? (total2 + G - 1) / G : 1;
+  s.it0 = gid * s.L < total2 ? gid * s.L : total2;
+  s.it1 = s.it0 + s.L < total2 ? s.it0 + s.L : total2;
   return s;
 }
 
