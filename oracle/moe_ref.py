@@ -93,6 +93,12 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
     score_mask = group_mask.unsqueeze(2).expand(T, N_GROUP, gsz).reshape(T, E_GLOBAL)
     pruned = s_with_bias.masked_fill(score_mask == 0, torch.finfo(torch.float32).min)
     topk_idx = torch.topk(pruned, k=TOP_K, dim=1, sorted=False).indices
+    return _route_weights(s, topk_idx, routed_scaling_factor)
+
+
+def _route_weights(s: torch.Tensor, topk_idx: torch.Tensor, routed_scaling_factor: float):
+    """Weights of the picked experts: s / (sum of the picked s + 1e-20) * scale,
+    summed as a dense [T,256] row (flashinfer ``moe.py:109-185``)."""
     M = torch.zeros_like(s)
     M.scatter_(1, topk_idx, 1.0)
     raw = s * M
@@ -100,6 +106,35 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
     topk_idx = topk_idx.sort(dim=1).values
     topk_w = dense_w.gather(1, topk_idx)
     return topk_idx, topk_w, dense_w
+
+
+def route_lowest_id_ties(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
+                         routed_scaling_factor: float):
+    """``route`` with ties resolved as the reference's CUDA routing kernel does.
+
+    ``torch.topk`` leaves the order of equal scores unspecified, so on inputs
+    with exact ties the definition picks an implementation-defined set.  The
+    reference's own kernel (``solution/python/kernel.cu:84-160``) keeps the
+    lower group when group scores tie (strict ``>`` scan, ``:101-110``) and the
+    lower expert id when scores tie (``__ffs`` of the ballot of equal lanes,
+    ``:117-130`` inside a group, ``:147-160`` across groups), i.e. a stable
+    descending sort.  Without ties this returns exactly what ``route`` does.
+    """
+    T = routing_logits.shape[0]
+    logits = routing_logits.to(torch.float32)
+    bias = routing_bias.to(torch.float32).reshape(-1)
+    s = 1.0 / (1.0 + torch.exp(-logits))
+    s_with_bias = s + bias
+    gsz = E_GLOBAL // N_GROUP
+    top2 = torch.topk(s_with_bias.view(T, N_GROUP, gsz), k=2, dim=2, sorted=True).values
+    group_scores = top2[..., 0] + top2[..., 1]
+    group_idx = torch.sort(group_scores, dim=1, descending=True, stable=True).indices[:, :TOPK_GROUP]
+    group_mask = torch.zeros_like(group_scores)
+    group_mask.scatter_(1, group_idx, 1.0)
+    score_mask = group_mask.unsqueeze(2).expand(T, N_GROUP, gsz).reshape(T, E_GLOBAL)
+    pruned = s_with_bias.masked_fill(score_mask == 0, -float("inf"))
+    topk_idx = torch.sort(pruned, dim=1, descending=True, stable=True).indices[:, :TOP_K]
+    return _route_weights(s, topk_idx, routed_scaling_factor)
 
 
 # --------------------------------------------------------------------------

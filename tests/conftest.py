@@ -54,3 +54,16 @@ def cached_inputs(T, E_l, offset, seed, skew=0.0):
 
 def load_golden(name):
     return torch.load(GOLDEN / f"{name}.pt", weights_only=True)
+
+
+def tied_routing_inputs(T: int, seed: int, bias_grid: bool = False):
+    """Routing inputs full of exact score ties: logits on a 0.5 grid in [-1, 1]
+    and a zero bias (or a bias on a 0.25 grid), so many experts and groups of a
+    token share one sigmoid-plus-bias value."""
+    g = torch.Generator().manual_seed(seed)
+    logits = torch.randint(-2, 3, (T, 256), generator=g).float() * 0.5
+    if bias_grid:
+        bias = (torch.randint(-1, 2, (256,), generator=g).float() * 0.25).to(torch.bfloat16)
+    else:
+        bias = torch.zeros(256, dtype=torch.bfloat16)
+    return logits, bias

@@ -89,8 +89,11 @@ def test_routing_matches_reference(name, pkg, cuda_dev):
     ids = torch.empty(T, 8, dtype=torch.int32, device=cuda_dev)
     w = torch.empty(T, 8, dtype=torch.float32, device=cuda_dev)
     _, L = _mods()
-    st = L.load().moe_fp8_ds_route(ctypes.c_void_p(logits.to(cuda_dev).data_ptr()),
-                                   ctypes.c_void_p(bias.to(cuda_dev).data_ptr()), T, ctypes.c_float(2.5),
+    # device copies held in names: a temporary's memory could go to the next
+    # allocation before the asynchronous launch reads it
+    logits_d, bias_d = logits.to(cuda_dev), bias.to(cuda_dev)
+    st = L.load().moe_fp8_ds_route(ctypes.c_void_p(logits_d.data_ptr()),
+                                   ctypes.c_void_p(bias_d.data_ptr()), T, ctypes.c_float(2.5),
                                    ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(w.data_ptr()),
                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     L.check(st, "moe_fp8_ds_route")
@@ -100,6 +103,30 @@ def test_routing_matches_reference(name, pkg, cuda_dev):
     frac1 = float((u <= 1).float().mean())
     print(f"{name}: weights ulp hist {[int((u == k).sum()) for k in range(5)]} max {int(u.max())}")
     assert frac1 >= 0.999 and int(u.max()) <= 4
+
+
+@pytest.mark.parametrize("T,seed,bias_grid", [(512, 0, False), (300, 1, True)])
+def test_routing_ties_break_toward_lowest_id(T, seed, bias_grid, pkg, oracle, cuda_dev):
+    """Exact score ties (logits on a 0.5 grid): ids must follow the reference CUDA
+    kernel's rule (lower group, then lower expert id), ``kernel.cu:84-160``."""
+    from conftest import tied_routing_inputs
+    logits, bias = tied_routing_inputs(T, seed, bias_grid)
+    ids = torch.empty(T, 8, dtype=torch.int32, device=cuda_dev)
+    w = torch.empty(T, 8, dtype=torch.float32, device=cuda_dev)
+    _, L = _mods()
+    # device copies held in names: a temporary's memory could go to the next
+    # allocation before the asynchronous launch reads it
+    logits_d, bias_d = logits.to(cuda_dev), bias.to(cuda_dev)
+    st = L.load().moe_fp8_ds_route(ctypes.c_void_p(logits_d.data_ptr()),
+                                   ctypes.c_void_p(bias_d.data_ptr()), T, ctypes.c_float(2.5),
+                                   ctypes.c_void_p(ids.data_ptr()), ctypes.c_void_p(w.data_ptr()),
+                                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+    L.check(st, "moe_fp8_ds_route")
+    torch.cuda.synchronize()
+    want_ids, want_w, _ = oracle.route_lowest_id_ties(logits, bias, 2.5)
+    assert torch.equal(ids.cpu(), want_ids.to(torch.int32)), "tie-breaking differs from the reference kernel"
+    u = ulp_distance(w.cpu(), want_w)
+    assert int(u.max()) <= 4 and float((u <= 1).float().mean()) >= 0.999
 
 
 # ---------------------------------------------------------------------------- golden
