@@ -145,7 +145,7 @@ def token_slice(base, T):
 def routing_stats(K, L, inp, T, E_l):
     """(active local experts, local assignments) of this batch, read from the workspace."""
     lay = K.workspace_layout(T, E_l)
-    ws = K._workspaces[torch.cuda.current_device()]
+    ws = K.workspace_for()
     seg = ws[lay.seg_offsets:lay.seg_offsets + 4 * (E_l + 1)].view(torch.int32).cpu()
     counts = seg[1:] - seg[:-1]
     return int((counts > 0).sum()), int(seg[-1])

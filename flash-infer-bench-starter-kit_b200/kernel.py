@@ -21,8 +21,14 @@ from . import _lib
 
 H, I, E_GLOBAL, TOP_K = 7168, 2048, 256, 8
 
+# One workspace per (device, stream): calls on one stream run in order, so they
+# can share a workspace; calls on different streams could overlap and get
+# their own.  Each is allocated on its stream, so dropping a smaller one when
+# it grows is ordered after that stream's earlier launches by torch's caching
+# allocator (the reference allocates its buffers per call the same way,
+# ``main.cpp:87-252``).
 _ws_lock = threading.Lock()
-_workspaces: dict[int, torch.Tensor] = {}     # device index -> uint8 workspace (grown on demand)
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}   # (device index, stream handle) -> uint8
 
 
 def workspace_bytes(num_tokens: int, num_local_experts: int) -> int:
@@ -41,16 +47,32 @@ def workspace_layout(num_tokens: int, num_local_experts: int) -> _lib.MoeLayout:
     return lay
 
 
+def _device_index(device: torch.device | None) -> int:
+    if device is None or device.index is None:
+        return torch.cuda.current_device()
+    return device.index
+
+
 def get_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """The per-device workspace, zero-filled on (re)allocation, at least ``nbytes`` long."""
-    idx = device.index if device.index is not None else torch.cuda.current_device()
+    """The workspace of ``device``'s current stream, zero-filled on (re)allocation and at
+    least ``nbytes`` long.  Launch the work that uses it on that same stream."""
+    idx = _device_index(device)
+    stream = torch.cuda.current_stream(idx)
+    key = (idx, stream.cuda_stream)
     with _ws_lock:
-        ws = _workspaces.get(idx)
+        ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
-            _workspaces.pop(idx, None)
-            ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
-            _workspaces[idx] = ws
+            _workspaces.pop(key, None)
+            with torch.cuda.device(idx), torch.cuda.stream(stream):
+                ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
+            _workspaces[key] = ws
         return ws
+
+
+def workspace_for(device: torch.device | None = None) -> torch.Tensor | None:
+    """The workspace last used on ``device``'s current stream, or None."""
+    idx = _device_index(device)
+    return _workspaces.get((idx, torch.cuda.current_stream(idx).cuda_stream))
 
 
 def _check_tensor(name, t, dtype, shape, device):
@@ -141,19 +163,21 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
 
 
 def read_device_error(device: torch.device | None = None) -> int:
-    """Synchronise the current stream and return (and clear) the device error code of the
-    workspace used on ``device``; 0 means no device-side error since the last read."""
+    """Synchronise the streams ``kernel(...)`` ran on for ``device`` and return (and clear)
+    their workspaces' device error codes: the first non-zero one, or 0 when no device-side
+    error happened since the last read."""
     lib = _lib.load()
-    dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    idx = dev.index if dev.index is not None else torch.cuda.current_device()
-    ws = _workspaces.get(idx)
-    if ws is None:
-        return 0
-    code = ctypes.c_int32(0)
+    idx = _device_index(device)
+    with _ws_lock:
+        mine = [(key[1], ws) for key, ws in _workspaces.items() if key[0] == idx]
+    first = 0
     with torch.cuda.device(idx):
-        st = lib.moe_fp8_ds_read_device_error(ctypes.c_void_p(ws.data_ptr()),
-                                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream),
-                                              ctypes.byref(code))
-    if st not in (_lib.MOE_OK, _lib.MOE_ERR_DEVICE_TIMEOUT, _lib.MOE_ERR_DEVICE_FAULT):
-        _lib.check(st, "moe_fp8_ds_read_device_error")
-    return int(code.value)
+        for stream, ws in mine:
+            code = ctypes.c_int32(0)
+            st = lib.moe_fp8_ds_read_device_error(ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(stream),
+                                                  ctypes.byref(code))
+            if st not in (_lib.MOE_OK, _lib.MOE_ERR_DEVICE_TIMEOUT, _lib.MOE_ERR_DEVICE_FAULT):
+                _lib.check(st, "moe_fp8_ds_read_device_error")
+            if first == 0:
+                first = int(code.value)
+    return first

@@ -251,6 +251,38 @@ def test_public_kernel_entry_and_device_error(pkg, oracle, cuda_dev):
     check_output(out, ref32)
 
 
+def test_streams_get_their_own_workspace(pkg, cuda_dev):
+    """Calls on two streams may overlap, so each stream keeps its own workspace; results
+    equal the same calls made one after the other, bit for bit."""
+    K, _ = _mods()
+    a = to_dev(cached_inputs(16, 8, 0, 12), cuda_dev)
+    b = to_dev(cached_inputs(64, 32, 0, 13), cuda_dev)
+    want_a = torch.empty(16, 7168, dtype=torch.bfloat16, device=cuda_dev)
+    want_b = torch.empty(64, 7168, dtype=torch.bfloat16, device=cuda_dev)
+    pkg.kernel(*pkg.inputs.as_args(a), want_a)
+    pkg.kernel(*pkg.inputs.as_args(b), want_b)
+    s1, s2 = torch.cuda.Stream(cuda_dev), torch.cuda.Stream(cuda_dev)
+    outs = []
+    for _ in range(3):
+        out_a = torch.empty_like(want_a)
+        out_b = torch.empty_like(want_b)
+        for s, inp, out in ((s1, a, out_a), (s2, b, out_b)):
+            s.wait_stream(torch.cuda.current_stream(cuda_dev))
+            with torch.cuda.stream(s):
+                pkg.kernel(*pkg.inputs.as_args(inp), out)
+        outs.append((out_a, out_b))
+    with torch.cuda.stream(s1):
+        ws1 = K.workspace_for(cuda_dev)
+    with torch.cuda.stream(s2):
+        ws2 = K.workspace_for(cuda_dev)
+    torch.cuda.synchronize(cuda_dev)
+    assert ws1 is not None and ws2 is not None and ws1.data_ptr() != ws2.data_ptr()
+    for out_a, out_b in outs:
+        assert torch.equal(out_a.view(torch.int16), want_a.view(torch.int16))
+        assert torch.equal(out_b.view(torch.int16), want_b.view(torch.int16))
+    assert K.read_device_error(cuda_dev) == 0
+
+
 def test_routed_entry_equals_full_entry(pkg, cuda_dev):
     K, L = _mods()
     inp = to_dev(cached_inputs(64, 32, 0, 13), cuda_dev)
