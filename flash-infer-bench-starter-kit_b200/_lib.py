@@ -61,7 +61,7 @@ EXPORTS = (
     "moe_fp8_ds_status_string", "moe_fp8_ds_launches_per_call", "moe_fp8_ds_set_tile_override",
     "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc", "moe_fp8_ds_set_path_override",
     "moe_fp8_ds_ep_plan", "moe_fp8_ds_ep_pack", "moe_fp8_ds_ep_unpack", "moe_fp8_ds_ep_combine",
-    "moe_fp8_ds_selftest_wait_timeout",
+    "moe_fp8_ds_selftest_wait_timeout", "moe_fp8_ds_noalloc_read_device_error",
 )
 
 _lib = None

@@ -29,7 +29,7 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
-int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs, 3 f16 on CTA pairs
+int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
 constexpr int kWideMinTokens = 1536;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
@@ -77,7 +77,6 @@ struct Plan {
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
   int bt1, bt2;                     // compiled tile width of each GEMM (>= bn: the tile cap)
   bool wide;                        // large batch: f16-operand GEMMs (gemm_f16.cu)
-  bool pair;                        // ... on CTA pairs (gemm_f16_pair.cu)
   uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2, front_sync;
 };
 
@@ -85,6 +84,14 @@ uint64_t align256(uint64_t x) { return (x + 255) & ~uint64_t(255); }
 
 void make_plan(int T, int E_l, int sm_count, Plan* P) {
   memset(P, 0, sizeof(*P));
+  // The tuning knobs may be changed by another thread: one snapshot per plan.
+  int bn_override[2], path_override;
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    bn_override[0] = g_bn_override[0];
+    bn_override[1] = g_bn_override[1];
+    path_override = g_path_override;
+  }
   P->T = T;
   P->E_l = E_l;
   P->NB = (T + kPermBlock - 1) / kPermBlock;
@@ -96,14 +103,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // f16-operand GEMMs win once experts see ~48+ tokens each (measured on B200
   // with 32 local experts, layer time e4m3 / f16: T=1024 381/414 us, 1536
   // 470/470, 2048 562/500, 3072 758/644, 16384 3047/2190).
-  P->wide = g_path_override >= 2 || (g_path_override == 0 && T >= kWideMinTokens);
-  P->pair = P->wide && g_path_override == 3;
-  int pair_grid1 = 0, pair_grid2 = 0;
-  if (P->pair) {
-    pair_grid1 = gemm_pair_grid(1, sm_count);
-    pair_grid2 = gemm_pair_grid(2, sm_count);
-    if (pair_grid1 < 2 || pair_grid2 < 2) P->pair = false;   // clusters of two not resident
-  }
+  P->wide = path_override >= 2 || (path_override == 0 && T >= kWideMinTokens);
   if (P->wide) {
     // f16 kernels accumulate in TMEM, so one tile takes up to 256 tokens.
     // The widest tiles win, measured on B200 with 32 local experts: each
@@ -118,20 +118,15 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
     const double per_expert = (double)T * kTopK / kExpertsGlobal;
     const int bn = per_expert >= 384.0 ? 256 : 128;
     const int bn_2 = 256;
-    P->bn1 = g_bn_override[0] ? g_bn_override[0] : bn;
-    P->bn2 = g_bn_override[1] ? g_bn_override[1] : bn_2;
+    P->bn1 = bn_override[0] ? bn_override[0] : bn;
+    P->bn2 = bn_override[1] ? bn_override[1] : bn_2;
     P->bt1 = P->bn1 > 128 ? 256 : 128;
     P->bt2 = P->bn2 > 128 ? 256 : 128;
-    if (P->pair) {   // one tile of up to 256 tokens per pair, two accumulators per CTA
-      P->bn1 = g_bn_override[0] ? g_bn_override[0] : 256;
-      P->bn2 = g_bn_override[1] ? g_bn_override[1] : 256;
-      P->bt1 = P->bt2 = 256;
-    }
   } else {
     // e4m3 kernels are compiled for 16, 32, 64 and 128 tokens only.
     auto compiled = [](int v) { return v == 16 || v == 32 || v == 64 || v == 128; };
-    P->bn1 = compiled(g_bn_override[0]) ? g_bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
-    P->bn2 = compiled(g_bn_override[1]) ? g_bn_override[1] : bn_auto;
+    P->bn1 = compiled(bn_override[0]) ? bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
+    P->bn2 = compiled(bn_override[1]) ? bn_override[1] : bn_auto;
     P->bt1 = P->bn1;
     P->bt2 = P->bn2;
   }
@@ -157,7 +152,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->tiles2 = take((uint64_t)P->max_mt2 * 16);
   P->sched = take(64);
   P->front_sync = take(16);
-  P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 2 * 4);   // x2: pair GEMM1 counts per CTA
+  P->counters1 = take((uint64_t)P->max_mt1 * (kInter / 128) * 4);
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->ready = take((uint64_t)E_l * 4);
   P->pub.row_token = take(R * 4);
@@ -169,12 +164,7 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.act16 = take(R16 * kHidden * 2);
   P->pub.inter16 = take(R16 * kInter * 2);
   P->pub.down = take(R * kHidden * 4);
-  if (P->pair) {
-    P->grid1 = pair_grid1;
-    P->grid2 = pair_grid2;
-    P->partials1 = take(gemm_pair_partials_bytes(P->grid1));
-    P->partials2 = take(gemm_pair_partials_bytes(P->grid2));
-  } else if (P->wide) {
+  if (P->wide) {
     P->grid1 = P->grid2 = sm_count;
     P->partials1 = take(gemm_f16_partials_bytes(1, P->bt1, P->grid1));
     P->partials2 = take(gemm_f16_partials_bytes(2, P->bt2, P->grid2));
@@ -290,15 +280,10 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   __half* inter16 = reinterpret_cast<__half*>(at(P.pub.inter16));
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
   if (P.wide) {
-    // pair kernels: each CTA loads 64 X1 + 64 X2 rows (GEMM1) or 128 rows
-    // (GEMM2) of weights and a 128-row half of the token tile
-    const uint32_t w1_rows = P.pair ? 64 : 128;
-    const uint32_t b1_rows = P.pair ? (uint32_t)P.bn1 / 2 : (uint32_t)P.bn1;
-    const uint32_t b2_rows = P.pair ? (uint32_t)P.bn2 / 2 : (uint32_t)P.bn2;
-    if (!encode_w8_atoms(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, w1_rows) ||
-        !encode_b16_atoms(&tm_b1, act16, kHidden, (uint64_t)P.R_cap, b1_rows) ||
+    if (!encode_w8_atoms(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out) ||
+        !encode_b16_atoms(&tm_b1, act16, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
         !encode_w8_atoms(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden) ||
-        !encode_b16_atoms(&tm_b2, inter16, kInter, (uint64_t)P.R_cap, b2_rows))
+        !encode_b16_atoms(&tm_b2, inter16, kInter, (uint64_t)P.R_cap, (uint32_t)P.bn2))
       return MOE_ERR_INVALID_ARGUMENT;
   } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
@@ -329,7 +314,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(1, s);
     ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
-                     P.pair ? 2 * (kInter / 128) : kInter / 128, cnt2, kHidden / 128, ready, s);
+                     kInter / 128, cnt2, kHidden / 128, ready, s);
     if (ce != cudaSuccess) return MOE_ERR_CUDA;
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
@@ -346,11 +331,10 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
   g1.inter16 = inter16;
-  g1.box_rows = P.pair ? P.bn1 / 2 : P.bn1;
+  g1.box_rows = P.bn1;
   g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
   g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
-  ce = P.pair   ? launch_gemm_pair(1, &tm_w1, &tm_b1, g1, P.grid1, s)
-       : P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
+  ce = P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
               : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
@@ -362,9 +346,8 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
   g2.inter16 = nullptr;
-  g2.box_rows = P.pair ? P.bn2 / 2 : P.bn2;
-  ce = P.pair   ? launch_gemm_pair(2, &tm_w2, &tm_b2, g2, P.grid2, s)
-       : P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
+  g2.box_rows = P.bn2;
+  ce = P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
               : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
   if (ce != cudaSuccess) return MOE_ERR_CUDA;
 
@@ -519,7 +502,7 @@ int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
 }
 
 int moe_fp8_ds_set_path_override(int32_t mode) {
-  if (mode < 0 || mode > 3) return MOE_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 2) return MOE_ERR_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lk(g_mu);
   g_path_override = mode;
   return MOE_OK;

@@ -92,12 +92,8 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
 // weight tile from L2 rather than from HBM again, and each expert's tiles finish
 // together (the early-start consumer waits per expert).
 __host__ __device__ __forceinline__ int2 unit_tile(int u, int n_mt, int NT) {
-#ifdef MOE_UNIT_NT_MAJOR
-  return make_int2(u % n_mt, u / n_mt);
-#else
   (void)n_mt;
   return make_int2(u / NT, u % NT);
-#endif
 }
 
 __device__ __forceinline__ void fence_proxy_async() {

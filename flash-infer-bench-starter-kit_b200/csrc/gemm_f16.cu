@@ -30,23 +30,6 @@
 
 namespace moe {
 
-#ifdef MOE_F16_TL
-// Diagnostics builds only: %globaltimer stamps of the first 256 pipeline
-// steps of CTA 0 of each GEMM, [kind][event][step].
-__device__ unsigned long long g_f16_tl[2][6][256];
-#define F16_TL(ev, i) do { if (blockIdx.x == 0 && (i) < 256) g_f16_tl[KIND - 1][ev][i] = globaltimer_ns(); } while (0)
-#else
-#define F16_TL(ev, i) ((void)0)
-#endif
-
-// Diagnostics builds only: drop the weight conversion (1) or the MMAs (2) to
-// see which stage bounds the pipeline.
-#ifndef MOE_F16_PROBE
-#define MOE_F16_PROBE 0
-#endif
-#ifndef MOE_F16_NCONV
-#define MOE_F16_NCONV 8
-#endif
 
 // Shared memory holds two rings:
 //   raw ring (RS stages): what TMA writes -- the e4m3 weight tile(s) and the
@@ -97,7 +80,7 @@ struct B16Cfg {
   // when they fit in TMEM's 512 columns, else one.
   static constexpr int NACC = 2 * ACC <= 512 ? 2 : 1;
   static constexpr int TMEM_COLS = NACC * ACC <= 128 ? 128 : NACC * ACC <= 256 ? 256 : 512;
-  static constexpr int NCONV = MOE_F16_NCONV;               // converter warps
+  static constexpr int NCONV = 8;               // converter warps
   static constexpr int EPI0 = 64 + 32 * NCONV;              // first epilogue thread
   static constexpr int THREADS = EPI0 + 128;
   static constexpr int CROWS = 128 / NCONV;                 // weight rows per converter warp
@@ -186,7 +169,6 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         const int4 tile = p.tiles[mt];
         const int s = i % RS;
         if (!mbar_wait_bounded(&empty[s], ((i / RS) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        F16_TL(0, i);
         mbar_arrive_expect_tx(&full[s], C::OFF_B + p.box_rows * 128);
         uint8_t* st = smem + s * C::RAW;
         // weights: e4m3 [rows][64 B] per tile (X1 then X2 for GEMM1)
@@ -229,7 +211,6 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         // so conv[o] also orders the token tile's TMA writes before the MMA.
         const int s = i % RS, o = i % OS;
         if (!mbar_wait_bounded(&conv[o], (i / OS) & 1, abort_flag)) { ok = false; break; }
-        F16_TL(4, i);
         tc_fence_after();
         const uint64_t bdesc = make_sdesc_sw128(smem_base + s * C::RAW + C::OFF_B);
         const uint32_t op = smem_base + C::OFF_OP + o * C::OPS;
@@ -238,7 +219,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
           const uint64_t adesc = make_sdesc_sw128(op + w * C::W16_TILE);
           const uint32_t d = tmem_base + (uint32_t)(b * C::ACC + w * BN);
 #pragma unroll
-          for (int k = 0; k < 4 * (MOE_F16_PROBE != 2); ++k)   // 4 x K=16 per 128-byte atom; +32 B = +2 in addr>>4
+          for (int k = 0; k < 4; ++k)   // 4 x K=16 per 128-byte atom; +32 B = +2 in addr>>4
             tc_mma_f16(d, adesc + 2 * k, bdesc + 2 * k, idesc, (seg_first && k == 0) ? 0u : 1u);
         }
         tc_commit(&empty[s]);
@@ -269,14 +250,12 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
         wsc[w] = __ldg(p.w_scale + ((size_t)e * (C::W_ROWS / 128) + nb) * (C::K / 128) + a / 2);
       }
       if (!mbar_wait_bounded(&full[s], (i / RS) & 1, abort_flag)) break;
-      if (q == 0 && lane == 0) F16_TL(1, i);
       if (!mbar_wait_bounded(&opempty[o], ((i / OS) & 1) ^ 1, abort_flag)) break;
-      if (q == 0 && lane == 0) F16_TL(2, i);
       const uint8_t* st = smem + s * C::RAW;
       uint8_t* opst = smem + C::OFF_OP + o * C::OPS;
       const int part = lane & 3;
 #pragma unroll
-      for (int w = 0; w < C::NW * (MOE_F16_PROBE != 1); ++w) {
+      for (int w = 0; w < C::NW; ++w) {
         uint4 src[C::CROWS / 8];
 #pragma unroll
         for (int rr = 0; rr < C::CROWS / 8; ++rr) {
@@ -296,7 +275,6 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&conv[o]);
-      if (q == 0 && lane == 0) F16_TL(3, i);
     }
     if (*abort_flag) raise_error(p.err, kDevTimeoutProducer);
   } else {
@@ -447,8 +425,3 @@ cudaError_t launch_gemm_f16(int kind, int bn, const CUtensorMap* tm_w, const CUt
 
 }  // namespace moe
 
-#ifdef MOE_F16_TL
-extern "C" __attribute__((visibility("default"))) int moe_probe_f16_timeline(unsigned long long* host) {
-  return cudaMemcpyFromSymbol(host, moe::g_f16_tl, sizeof(moe::g_f16_tl)) == cudaSuccess ? 0 : 1;
-}
-#endif

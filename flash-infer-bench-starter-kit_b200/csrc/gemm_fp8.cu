@@ -46,18 +46,6 @@
 
 namespace moe {
 
-#ifndef MOE_GEMM_PROBE_NOEPI
-#define MOE_GEMM_PROBE_NOEPI 0   // diagnostics builds only: skip the promotion arithmetic
-#endif
-
-#ifdef MOE_GEMM_TIMELINE
-// Diagnostics builds only: per-CTA %globaltimer stamps of pipeline milestones.
-__device__ unsigned long long g_timeline[2][1024][8];
-#define MOE_TL(ev) g_timeline[KIND - 1][blockIdx.x][ev] = globaltimer_ns()
-#else
-#define MOE_TL(ev) ((void)0)
-#endif
-
 template <int KIND, int BN, int STAGES, int NWG, int KS, int OCC = 1>
 struct GemmCfg {
   static constexpr int NW = KIND == 1 ? 2 : 1;              // weight tiles per K block
@@ -113,7 +101,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) MOE_TL(0);
   // GEMM1 waits for the routing/permutation kernels -- after the fused front
   // kernel only for its tile lists (front_sync[0]), so the weight stream starts
   // while the front kernel still gathers activations (front_sync[1] counts
@@ -134,7 +121,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
   } else if (KIND == 1 || !p.early_start) {
     griddep_wait();
   }
-  if (threadIdx.x == 0) MOE_TL(1);
   griddep_launch_dependents();
   const WorkSched sch = make_work_sched(p.sched[KIND - 1], C::NT, C::KSTEPS);
   const int n_iter = sch.n_iter();
@@ -220,7 +206,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           idesc = make_idesc_f8(128, min(C::MMA_N, (rows + 15) & ~15));
         }
         if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
-        if (i == 0) MOE_TL(2);
         if (!mbar_wait_bounded(&tempty[b], ((i / C::NBUF) & 1) ^ 1, abort_flag)) { ok = false; break; }
         tc_fence_after();
         const uint32_t st = smem_base + s * C::STAGE;
@@ -239,7 +224,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         tc_commit(&empty[s]);
         tc_commit(&tfull[b]);
       }
-      MOE_TL(3);
       if (!ok) raise_error(p.err, kDevTimeoutMma);
       // Wait for every MMA this thread issued before TMEM is released.
       tc_commit(drain);
@@ -318,7 +302,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (got) {
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < KS * (MOE_GEMM_PROBE_NOEPI == 0); ++kk) {
+        for (int kk = 0; kk < KS; ++kk) {
 #pragma unroll
           for (int w = 0; w < C::NW; ++w) {
             const float* coef = sl + (kk * C::NW + w) * BN + j0;
@@ -371,7 +355,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       if (named_bar_or(1, C::NEPI, *abort_flag != 0)) break;   // uniform abort decision
 
       const bool seg_last = (ks == C::KSTEPS - 1) || (i == n_iter - 1);
-      if (et == 0 && i == n_iter - 1) MOE_TL(6);
       if (!seg_last) continue;
 
       // ---------------- end of this CTA's share of unit u
@@ -393,7 +376,6 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
         }
         named_bar_sync(1, C::NEPI);
-        if (et == 0 && i == n_iter - 1) MOE_TL(7);
         if (!last_flag[0]) continue;
         __threadfence();
         if (c_hi - c_lo == 1) {
@@ -478,13 +460,11 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
       }
     }
-    if (et == 0) MOE_TL(4);
     if (*abort_flag) raise_error(p.err, kDevTimeoutEpilogue);
   }
 
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) MOE_TL(5);
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
@@ -496,24 +476,12 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 // Host-side dispatch: (kind, BN) -> stages, warpgroups, K blocks per stage.
 // --------------------------------------------------------------------------
 template <int KIND, int BN> struct Pick;
-#ifndef MOE_P116_S
-#define MOE_P116_S 3
-#define MOE_P116_K 2
-#endif
-#ifndef MOE_P216_S
-#define MOE_P216_S 2   // four K blocks per stage: 64 KB weight boxes (T=64: GEMM2 58 -> 51 us)
-#define MOE_P216_K 4
-#endif
-#ifndef MOE_P232_S
-#define MOE_P232_S 2   // likewise for 32-token tiles (T=600: GEMM2 124 -> 98 us)
-#define MOE_P232_K 4
-#endif
-template <> struct Pick<1, 16> { static constexpr int S = MOE_P116_S, W = 1, K = MOE_P116_K, O = 1; };
+template <> struct Pick<1, 16> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<1, 32> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<1, 64> { static constexpr int S = 2, W = 2, K = 2, O = 1; };
 template <> struct Pick<1, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
-template <> struct Pick<2, 16> { static constexpr int S = MOE_P216_S, W = 1, K = MOE_P216_K, O = 1; };
-template <> struct Pick<2, 32> { static constexpr int S = MOE_P232_S, W = 1, K = MOE_P232_K, O = 1; };
+template <> struct Pick<2, 16> { static constexpr int S = 2, W = 1, K = 4, O = 1; };
+template <> struct Pick<2, 32> { static constexpr int S = 2, W = 1, K = 4, O = 1; };
 template <> struct Pick<2, 64> { static constexpr int S = 3, W = 1, K = 2, O = 1; };
 template <> struct Pick<2, 128> { static constexpr int S = 4, W = 2, K = 1, O = 1; };
 
@@ -568,8 +536,3 @@ cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtenso
 
 }  // namespace moe
 
-#ifdef MOE_GEMM_TIMELINE
-extern "C" __attribute__((visibility("default"))) int moe_probe_timeline(unsigned long long* host) {
-  return cudaMemcpyFromSymbol(host, moe::g_timeline, sizeof(moe::g_timeline)) == cudaSuccess ? 0 : 1;
-}
-#endif

@@ -98,13 +98,6 @@ int gemm_ctas_per_sm(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st);
 
-// f16-operand GEMMs on CTA pairs (gemm_f16_pair.cu): 0 from gemm_pair_grid
-// means clusters of two cannot be resident.
-int gemm_pair_grid(int kind, int sm_count);
-size_t gemm_pair_partials_bytes(int grid);
-cudaError_t launch_gemm_pair(int kind, const CUtensorMap* tm_w, const CUtensorMap* tm_b, const GemmParams& p,
-                             int grid, cudaStream_t st);
-
 // f16-operand GEMMs for large batches (gemm_f16.cu).
 size_t gemm_f16_partials_bytes(int kind, int bn, int grid);
 cudaError_t launch_gemm_f16(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,

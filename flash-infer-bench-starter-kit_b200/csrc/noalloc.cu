@@ -24,21 +24,46 @@ constexpr int kNoAllocMaxDevices = 64;
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
 
 std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[kNoAllocMaxDevices] = {};
+struct ScratchSlot {
+  void* ctx = nullptr;    // CUcontext the address below belongs to
+  void* ptr = nullptr;    // device address of g_noalloc_scratch in that context
+};
+ScratchSlot g_noalloc_slot[kNoAllocMaxDevices];
 
-// Device address of the scratch array on the current device (looked up once
-// per device; the array's host-side name is not a device address).
-int scratch_address(void** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+
+// Set-up, once per device and context: the device address of the scratch
+// array on the current device (the array's host-side name is not a device
+// address), and a zeroed error block.  A context re-created after
+// cudaDeviceReset reloads this library's module, so the address is looked up
+// again for the new context.
+int scratch_address(cudaStream_t stream, void** out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices)
     return MOE_ERR_NO_DEVICE;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return MOE_ERR_CUDA;
-    g_noalloc_ptr[dev] = p;
+  if (!g_ctx_get_current) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return MOE_ERR_NO_DEVICE;
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
   }
-  *out = g_noalloc_ptr[dev];
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return MOE_ERR_NO_DEVICE;
+  ScratchSlot& slot = g_noalloc_slot[dev];
+  if (!ctx || slot.ctx != static_cast<void*>(ctx) || !slot.ptr) {
+    void* p = nullptr;
+    // Also makes the device's primary context current if none was.
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return MOE_ERR_CUDA;
+    if (g_ctx_get_current(&ctx) != CUDA_SUCCESS || !ctx) return MOE_ERR_NO_DEVICE;
+    if (cudaMemsetAsync(p, 0, 16, stream) != cudaSuccess) return MOE_ERR_CUDA;
+    slot.ctx = ctx;
+    slot.ptr = p;
+  }
+  *out = slot.ptr;
   return MOE_OK;
 }
 
@@ -55,11 +80,20 @@ extern "C" int moe_fp8_ds_run_noalloc(const moe_fp8_ds_args* args, void* stream)
   int st = moe_fp8_ds_workspace_size(args->num_tokens, args->num_local_experts, &need);
   if (st != MOE_OK) return st;
   if (need > kNoAllocScratchBytes) return MOE_ERR_TOO_LARGE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   void* ws = nullptr;
-  st = scratch_address(&ws);
+  st = scratch_address(s, &ws);
   if (st != MOE_OK) return st;
-  // The error word must start at zero; the rest is rewritten by every call.
-  if (cudaMemsetAsync(ws, 0, 16, static_cast<cudaStream_t>(stream)) != cudaSuccess)
-    return MOE_ERR_CUDA;
+  // Words 1..3 of the error block (grid-barrier state) must start at zero;
+  // word 0, the device error code, stays set until it is read.
+  if (cudaMemsetAsync(static_cast<int*>(ws) + 1, 0, 12, s) != cudaSuccess) return MOE_ERR_CUDA;
   return run_layer_with_workspace(args, ws, kNoAllocScratchBytes, stream, false);
+}
+
+extern "C" int moe_fp8_ds_noalloc_read_device_error(void* stream, int32_t* device_error) {
+  if (!device_error) return MOE_ERR_INVALID_ARGUMENT;
+  void* ws = nullptr;
+  const int st = scratch_address(static_cast<cudaStream_t>(stream), &ws);
+  if (st != MOE_OK) return st;
+  return moe_fp8_ds_read_device_error(ws, stream, device_error);
 }

@@ -11,14 +11,6 @@
 
 namespace moe {
 
-#ifdef MOE_GEMM_TIMELINE
-// Diagnostics builds only: per-CTA %globaltimer stamps of the front end.
-__device__ unsigned long long g_front_timeline[64][8];
-#define MOE_FTL(ev) if (threadIdx.x == 0) g_front_timeline[blockIdx.x & 63][ev] = globaltimer_ns()
-#else
-#define MOE_FTL(ev) ((void)0)
-#endif
-
 // --------------------------------------------------------------------------
 // Routing + per-block token masks of local experts.
 //
@@ -62,7 +54,6 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
       s[j] = __frcp_rn(__fadd_rn(1.0f, e));
       sb[j] = __fadd_rn(s[j], __bfloat162float(bb[j]));
     }
-    MOE_FTL(6);
     // ---- group score: sum of the top-2 sb of each 32-expert group
     float m1 = -INFINITY, m2 = -INFINITY;
 #pragma unroll
@@ -132,7 +123,6 @@ __device__ __forceinline__ int route_token(int t, int lane, const float* __restr
         bj = local_best();
       }
     }
-    MOE_FTL(7);
     // ---- sort the 8 picks ascending (all lanes hold the same arrays)
 #pragma unroll
     for (int a = 1; a < kTopK; ++a)
@@ -497,9 +487,7 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   __shared__ int s_n;
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
-  MOE_FTL(0);
   griddep_wait();
-  MOE_FTL(1);
   // GEMM1 is released only after the grid barrier below, so it cannot see the
   // previous call's flags: they are cleared here, before CTA 0 reaches it.
   if (blockIdx.x == 0 && threadIdx.x == 0) {
@@ -522,7 +510,6 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   }
   __syncthreads();
   store_masks(masks8, NB8p, E_l, s_mask);
-  MOE_FTL(2);
   // Up to eight CTAs run as one thread-block cluster (launch attribute) and
   // meet at the hardware cluster barrier, which also orders their global
   // writes (release/acquire at cluster scope); larger grids use the bounded
@@ -536,7 +523,6 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     return;
   }
   griddep_launch_dependents();
-  MOE_FTL(3);
   // ---- phase 2: per-expert counts and this CTA's first row per expert
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
     const unsigned int* row = reinterpret_cast<const unsigned int*>(masks8 + (size_t)e * NB8p);
@@ -591,7 +577,6 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
       atomicExch(front_sync, 1);
     }
   }
-  MOE_FTL(4);
   // ---- phase 3: rows of own tokens, inverse map, activation gather
   if (threadIdx.x < kRouteTokens * kTopK) {
     const int w8 = threadIdx.x / kTopK, k = threadIdx.x % kTopK;
@@ -641,7 +626,6 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     __threadfence();
     atomicAdd(front_sync + 1, 1);
   }
-  MOE_FTL(5);
 }
 
 // --------------------------------------------------------------------------
@@ -807,8 +791,3 @@ cudaError_t launch_combine(const float* down, const int32_t* inv_row, const floa
 
 }  // namespace moe
 
-#ifdef MOE_GEMM_TIMELINE
-extern "C" __attribute__((visibility("default"))) int moe_probe_front_timeline(unsigned long long* host) {
-  return cudaMemcpyFromSymbol(host, moe::g_front_timeline, sizeof(moe::g_front_timeline)) == cudaSuccess ? 0 : 1;
-}
-#endif

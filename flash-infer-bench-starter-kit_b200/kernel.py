@@ -26,9 +26,22 @@ H, I, E_GLOBAL, TOP_K = 7168, 2048, 256, 8
 # their own.  Each is allocated on its stream, so dropping a smaller one when
 # it grows is ordered after that stream's earlier launches by torch's caching
 # allocator (the reference allocates its buffers per call the same way,
-# ``main.cpp:87-252``).
+# ``main.cpp:87-252``).  A workspace lives until ``release_workspaces`` drops
+# it.  Next to it the entry keeps an event recorded after the last call that
+# used it, so the device error word can be read without touching the stream
+# itself (which the caller may have destroyed since).
 _ws_lock = threading.Lock()
-_workspaces: dict[tuple[int, int], torch.Tensor] = {}   # (device index, stream handle) -> uint8
+
+
+class _Workspace:
+    __slots__ = ("buf", "event")
+
+    def __init__(self, buf: torch.Tensor):
+        self.buf = buf
+        self.event = torch.cuda.Event()
+
+
+_workspaces: dict[tuple[int, int], _Workspace] = {}   # (device index, stream handle) -> workspace
 
 
 def workspace_bytes(num_tokens: int, num_local_experts: int) -> int:
@@ -53,26 +66,46 @@ def _device_index(device: torch.device | None) -> int:
     return device.index
 
 
-def get_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
-    """The workspace of ``device``'s current stream, zero-filled on (re)allocation and at
-    least ``nbytes`` long.  Launch the work that uses it on that same stream."""
+def _entry(device: torch.device, nbytes: int) -> _Workspace:
     idx = _device_index(device)
     stream = torch.cuda.current_stream(idx)
     key = (idx, stream.cuda_stream)
     with _ws_lock:
-        ws = _workspaces.get(key)
-        if ws is None or ws.numel() < nbytes:
+        ent = _workspaces.get(key)
+        if ent is None or ent.buf.numel() < nbytes:
             _workspaces.pop(key, None)
             with torch.cuda.device(idx), torch.cuda.stream(stream):
-                ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=torch.device("cuda", idx))
-            _workspaces[key] = ws
-        return ws
+                ent = _Workspace(torch.zeros(max(nbytes, 256), dtype=torch.uint8,
+                                             device=torch.device("cuda", idx)))
+            _workspaces[key] = ent
+        return ent
+
+
+def get_workspace(device: torch.device, nbytes: int) -> torch.Tensor:
+    """The workspace of ``device``'s current stream, zero-filled on (re)allocation and at
+    least ``nbytes`` long.  Launch the work that uses it on that same stream."""
+    return _entry(device, nbytes).buf
 
 
 def workspace_for(device: torch.device | None = None) -> torch.Tensor | None:
     """The workspace last used on ``device``'s current stream, or None."""
     idx = _device_index(device)
-    return _workspaces.get((idx, torch.cuda.current_stream(idx).cuda_stream))
+    ent = _workspaces.get((idx, torch.cuda.current_stream(idx).cuda_stream))
+    return ent.buf if ent is not None else None
+
+
+def release_workspaces(device: torch.device | None = None, stream: torch.cuda.Stream | None = None) -> int:
+    """Drop cached workspaces and return how many were dropped: all of them, those of
+    ``device``, or the one of ``stream``.  The memory goes back to torch's caching
+    allocator, ordered after the work already enqueued on each workspace's stream; the
+    next call on a released stream allocates (and zero-fills) a new workspace."""
+    with _ws_lock:
+        keys = [k for k in _workspaces
+                if (device is None or k[0] == _device_index(device))
+                and (stream is None or k[1] == stream.cuda_stream)]
+        for k in keys:
+            del _workspaces[k]
+    return len(keys)
 
 
 def _check_tensor(name, t, dtype, shape, device):
@@ -157,25 +190,29 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                       local_expert_offset, routed_scaling_factor, output)
     with torch.cuda.device(hidden_states.device):
-        ws = get_workspace(hidden_states.device,
-                           workspace_bytes(args.num_tokens, args.num_local_experts))
-        run_with_workspace(args, ws)
+        ent = _entry(hidden_states.device, workspace_bytes(args.num_tokens, args.num_local_experts))
+        run_with_workspace(args, ent.buf)
+        ent.event.record()
 
 
 def read_device_error(device: torch.device | None = None) -> int:
-    """Synchronise the streams ``kernel(...)`` ran on for ``device`` and return (and clear)
-    their workspaces' device error codes: the first non-zero one, or 0 when no device-side
-    error happened since the last read."""
+    """Wait for the last ``kernel(...)`` call on each of ``device``'s workspaces and return
+    (and clear) their device error codes: the first non-zero one, or 0 when no device-side
+    error happened since the last read.  The reads run on the current stream after it has
+    waited on each workspace's last-use event, so streams the caller has destroyed since
+    are never touched."""
     lib = _lib.load()
     idx = _device_index(device)
     with _ws_lock:
-        mine = [(key[1], ws) for key, ws in _workspaces.items() if key[0] == idx]
+        mine = [ent for key, ent in _workspaces.items() if key[0] == idx]
     first = 0
     with torch.cuda.device(idx):
-        for stream, ws in mine:
+        cur = torch.cuda.current_stream(idx)
+        for ent in mine:
+            cur.wait_event(ent.event)
             code = ctypes.c_int32(0)
-            st = lib.moe_fp8_ds_read_device_error(ctypes.c_void_p(ws.data_ptr()), ctypes.c_void_p(stream),
-                                                  ctypes.byref(code))
+            st = lib.moe_fp8_ds_read_device_error(ctypes.c_void_p(ent.buf.data_ptr()),
+                                                  ctypes.c_void_p(cur.cuda_stream), ctypes.byref(code))
             if st not in (_lib.MOE_OK, _lib.MOE_ERR_DEVICE_TIMEOUT, _lib.MOE_ERR_DEVICE_FAULT):
                 _lib.check(st, "moe_fp8_ds_read_device_error")
             if first == 0:

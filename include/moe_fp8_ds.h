@@ -130,14 +130,22 @@ MOE_API int moe_fp8_ds_run_routed(const moe_fp8_ds_args* args, void* workspace,
  * memory where they call the layer (an external memory manager owns all
  * allocations, or cudaMalloc is not allowed on the serving path).  No
  * counterpart in the reference.  Same arguments and result as
- * moe_fp8_ds_run, but the workspace is a 16 MiB array inside this library
- * that every GPU loading the library keeps until the process exits; T is
- * limited to 16 tokens (MOE_ERR_TOO_LARGE beyond).  The first call on a
- * device looks up that array's device address, so make it before any stream
- * capture.  All calls on a device share the array: calls that overlap on the
- * GPU (different streams, or threads) race and must be serialised by the
- * caller.  Device-side errors are not reported by this entry point.        */
+ * moe_fp8_ds_run (bit for bit: the same kernels on the same plan), but the
+ * workspace is a 16 MiB array inside this library that every GPU loading the
+ * library keeps until the process exits; T is limited to 16 tokens
+ * (MOE_ERR_TOO_LARGE beyond).  The first call on a device (and context) looks
+ * up that array's device address and zeroes its error block, so make it
+ * before any stream capture.  All calls on a device share the array: calls
+ * that overlap on the GPU (different streams, or threads) race and must be
+ * serialised by the caller.  A device-side error of any call stays recorded
+ * until moe_fp8_ds_noalloc_read_device_error reads it.                     */
 MOE_API int moe_fp8_ds_run_noalloc(const moe_fp8_ds_args* args, void* stream);
+
+/* Synchronises `stream`, reads and clears the device error word of the
+ * allocation-free entry point's built-in workspace (as
+ * moe_fp8_ds_read_device_error does for a caller's workspace).  No
+ * counterpart in the reference.                                            */
+MOE_API int moe_fp8_ds_noalloc_read_device_error(void* stream, int32_t* device_error);
 
 /* Routing only: writes ids (ascending per token) and weights.              */
 MOE_API int moe_fp8_ds_route(const float* routing_logits, const void* routing_bias, int32_t num_tokens,
@@ -169,9 +177,8 @@ MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Tuning knob: 0 = automatic GEMM family (e4m3 block-promotion GEMMs for
  * T < 1536, f16-operand TMEM-accumulating GEMMs from 1536 tokens), 1 = always
- * e4m3, 2 = always f16, 3 = always f16 on CTA pairs (cta_group::2, M = 256;
- * correct but measured slower, never chosen automatically).  Takes effect for
- * the next call (workspace size included). */
+ * e4m3, 2 = always f16.  Takes effect for the next call (workspace size
+ * included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);
 
 /* Profiling hook: when `count` is 7, later calls on this process record

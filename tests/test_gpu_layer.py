@@ -33,7 +33,7 @@ def to_dev(inp, dev):
 
 def run_layer(pkg, inp_dev, ws=None, bn=(0, 0), path=0):
     """Run through the C ABI with an explicit workspace; returns (output, ws, layout).
-    ``bn`` forces the token-tile widths, ``path`` the GEMM family (1 e4m3, 2 f16, 3 f16 on CTA pairs)."""
+    ``bn`` forces the token-tile widths, ``path`` the GEMM family (1 e4m3, 2 f16)."""
     K, L = _mods()
     lib = L.load()
     L.check(lib.moe_fp8_ds_set_tile_override(int(bn[0]), int(bn[1])), "set_tile_override")
@@ -162,10 +162,6 @@ STAGE_CASES = [
     (4200, 8, 0, 17, 0.0, (96, 176, 2)),   # f16 GEMMs, tile caps below the compiled widths
     (4200, 8, 0, 17, 0.0, (208, 0, 2)),    # f16 GEMM1 with 256-token tiles (one TMEM accumulator)
     (2100, 8, 0, 18, 3.0, (0, 0, 2)),      # f16 GEMMs, skewed routing: hot experts with many tiles
-    (300, 8, 0, 16, 0.0, (0, 0, 3)),       # f16 GEMMs on CTA pairs, small batch
-    (4200, 8, 0, 17, 0.0, (0, 0, 3)),      # f16 GEMMs on CTA pairs, 256-token tiles
-    (4200, 8, 0, 17, 0.0, (96, 176, 3)),   # CTA pairs with tile caps below 256
-    (2100, 8, 0, 18, 3.0, (0, 0, 3)),      # CTA pairs under skewed routing
 ]
 
 

@@ -78,9 +78,9 @@ def test_argument_validation_without_gpu(pkg):
     assert lib.moe_fp8_ds_ep_combine(None, None, 0, 2, None, None) == L.MOE_OK
     assert lib.moe_fp8_ds_ep_combine(None, None, 4, 9, None, None) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_tile_override(0, 0) == L.MOE_OK
-    assert lib.moe_fp8_ds_set_path_override(4) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_set_path_override(3) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_path_override(-1) == L.MOE_ERR_INVALID_ARGUMENT
-    assert lib.moe_fp8_ds_set_path_override(3) == L.MOE_OK
+    assert lib.moe_fp8_ds_set_path_override(2) == L.MOE_OK
     assert lib.moe_fp8_ds_set_path_override(0) == L.MOE_OK
 
 
@@ -95,3 +95,26 @@ def test_python_entry_rejects_cpu_tensors(pkg):
     with pytest.raises(ValueError):
         pkg.kernel(*[torch.zeros(1)] * 2, torch.zeros(1, 7168).to(torch.float8_e4m3fn),
                    *[torch.zeros(1)] * 5, 0, 2.5, torch.zeros(1, 7168, dtype=torch.bfloat16))
+
+
+def test_release_workspaces_drops_entries(pkg):
+    """Workspaces live per (device, stream) until released; release by stream, by
+    device and all at once (bookkeeping only, no GPU memory is touched)."""
+    K = sys.modules["fib_b200.kernel"]
+    saved = dict(K._workspaces)
+    try:
+        K._workspaces.clear()
+        for key in ((0, 11), (0, 12), (1, 13)):
+            K._workspaces[key] = K._Workspace(torch.zeros(256, dtype=torch.uint8))
+
+        class FakeStream:
+            cuda_stream = 12
+        assert K.release_workspaces(torch.device("cuda", 0), FakeStream()) == 1
+        assert set(K._workspaces) == {(0, 11), (1, 13)}
+        assert K.release_workspaces(torch.device("cuda", 1)) == 1
+        assert set(K._workspaces) == {(0, 11)}
+        assert K.release_workspaces() == 1
+        assert not K._workspaces
+    finally:
+        K._workspaces.clear()
+        K._workspaces.update(saved)
