@@ -56,7 +56,8 @@ def parse_args():
                         "reference-gpu: the reference's own CUTLASS GPU pipeline, prebuilt by "
                         "oracle/build_ref_gpu.py, timed on the same workloads (side comparison)")
     p.add_argument("--tokens", type=int, default=64, help="headline T")
-    p.add_argument("--sweep", default="1,16,1024,4096", help="extra T values ('' for none)")
+    p.add_argument("--sweep", default="1,16,1024,4096,16384s",
+                   help="extra T values ('' for none); a trailing 's' marks the skewed stress batch")
     p.add_argument("--local-experts", type=int, default=32)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
@@ -81,6 +82,22 @@ def measured_tensor_peak():
 
 
 WIDE_MIN_TOKENS = 1536      # the library switches to the f16-operand GEMMs here (api.cu)
+BENCH_BASE_TOKENS = 4096    # decode and prefill points are the first T tokens of one seeded batch
+SKEW_TOKENS = 16384         # BASELINE config 4 (skewed stress), one GPU's slice: 32 local experts
+SKEW_BOOST = 3.0            # added to the logits of the 16 hot experts (0-7, 32-39)
+
+
+def parse_sweep(spec):
+    """'1,16,1024,4096,16384s' -> [(1, False), ..., (16384, True)]; a trailing 's'
+    marks the skewed stress batch."""
+    if spec in ("", "none"):
+        return []
+    out = []
+    for x in spec.split(","):
+        x = x.strip()
+        if x:
+            out.append((int(x.rstrip("s")), x.endswith("s")))
+    return out
 
 
 def workload_name(T, E_l):
@@ -135,11 +152,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------- workload
 def token_slice(base, T):
     """Token-side inputs for T tokens cut from a larger seeded batch; weights shared."""
-    d = dict(base)
-    d["routing_logits"] = base["routing_logits"][:T].contiguous()
-    d["hidden_states"] = base["hidden_states"][:T].contiguous()
-    d["hidden_states_scale"] = base["hidden_states_scale"][:, :T].contiguous()
-    return d
+    return graft.load_package().inputs.token_slice(base, T)
 
 
 def routing_stats(K, L, inp, T, E_l):
@@ -257,7 +270,13 @@ def run_reference_arm(a, T, E_l):
     from oracle import moe_ref
     pkg = graft.load_package()
     torch.set_num_threads(os.cpu_count() or 1)
-    inp = pkg.inputs.make_inputs(T, E_l=E_l, seed=0)
+    # the GPU arm's batch: drawn on the GPU from seed 0 (the same generator and
+    # slice as the GPU arm's), then copied to the host cores that time it
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    base = pkg.inputs.bench_batch(BENCH_BASE_TOKENS, device=dev) if E_l == 32 else \
+        pkg.inputs.make_inputs(BENCH_BASE_TOKENS, E_l=E_l, seed=0, device=dev)
+    inp = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in token_slice(base, max(T, 1)).items()}
+    del base
     args = pkg.inputs.as_args(inp)
     for _ in range(a.warmup):
         moe_ref.moe_forward(*args)
@@ -411,9 +430,9 @@ def run_reference_gpu_arm(a, T, E_l):
     from oracle import moe_ref
     pkg = graft.load_package()
     dev = torch.device("cuda", 0)
-    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep not in ("", "none") else []
-    base_cpu = pkg.inputs.make_inputs(max([T] + sweep_T), E_l=E_l, seed=0)
-    base = {k: (v.to(dev) if torch.is_tensor(v) else v) for k, v in base_cpu.items()}
+    sweep_T = [t for t, skewed in parse_sweep(a.sweep) if not skewed]
+    base = pkg.inputs.bench_batch(max([T, BENCH_BASE_TOKENS] + sweep_T), device=dev)
+    base_cpu = {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in token_slice(base, T).items()}
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     def timed(Tm, impl):
@@ -426,7 +445,7 @@ def run_reference_gpu_arm(a, T, E_l):
 
     ms_ref, out_ref = timed(T, "ref")
     ms_ours, out_ours = timed(T, "ours")
-    ref32 = moe_ref.moe_forward(*pkg.inputs.as_args(token_slice(base_cpu, T)), return_fp32=True)
+    ref32 = moe_ref.moe_forward(*pkg.inputs.as_args(base_cpu), return_fp32=True)
 
     def err(o):
         d = (o.float().cpu() - ref32).abs()
@@ -481,15 +500,14 @@ def main():
     L = sys.modules["fib_b200._lib"]
     hbm_peak, peak_kind = measured_peaks()
 
-    sweep_T = [int(x) for x in a.sweep.split(",") if x.strip()] if a.sweep not in ("", "none") else []
-    T_max = max([T] + sweep_T)
-    # Each rank holds the 32 experts of one expert-parallel slot (offset 32*rank).
-    offset = (E_l * rank) % 256
-    base = pkg.inputs.make_inputs(T_max, E_l=E_l, local_expert_offset=offset, seed=rank, device=dev)
+    sweep_T = parse_sweep(a.sweep)
+    base = pkg.inputs.bench_batch(max(BENCH_BASE_TOKENS, T), device=dev) if E_l == 32 else \
+        pkg.inputs.make_inputs(max(BENCH_BASE_TOKENS, T), E_l=E_l, seed=0, device=dev)
+    skew_base = None
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
-    def measure(Tm, steps, warmup):
-        inp = token_slice(base, Tm)
+    def measure(Tm, steps, warmup, src=None):
+        inp = token_slice(base if src is None else src, Tm)
         out = torch.empty(Tm, H, dtype=torch.bfloat16, device=dev)
         fn = lambda: pkg.kernel(*pkg.inputs.as_args(inp), out)  # noqa: E731
         ts = time_steps(fn, steps, warmup, flush)
@@ -498,17 +516,11 @@ def main():
 
     # ---- headline
     inp, fn, ts, n_act, R = measure(T, a.warmup, a.warmup)     # warm everything once
-    if world > 1:
-        torch.distributed.barrier()
     torch.cuda.synchronize()
     clk = ClockSampler(local_rank).__enter__()
     ts = time_steps(fn, a.steps, a.warmup, flush)
     ms = sum(ts) / len(ts)
-    if world > 1:
-        t = torch.tensor([ms], device=dev)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t)
-    value = T * world / (ms * 1e-3)
+    value = T / (ms * 1e-3)
     stages = stage_times(L, fn, max(3, min(a.steps, 10)), flush)
     ab = algorithmic_bytes(T, n_act, R)
     dom = max(("gemm1", "gemm2"), key=lambda s: stages[s])
@@ -516,21 +528,30 @@ def main():
     e2e_ms, h2d, d2h = e2e_steps(pkg, inp, T, a.steps, a.warmup)
 
     sweep = []
-    for Ts in sweep_T:
-        _, _, tss, na, Rs = measure(Ts, a.steps, a.warmup)
+    for Ts, skewed in sweep_T:
+        src = None
+        if skewed:
+            if skew_base is None:     # BASELINE config 4 on one GPU: its own seeded skewed batch
+                skew_base = pkg.inputs.bench_batch(max(SKEW_TOKENS, Ts), skew=SKEW_BOOST, device=dev)
+            src = skew_base
+        _, fns, tss, na, Rs = measure(Ts, a.steps, a.warmup, src)
         mss = sum(tss) / len(tss)
         bb = algorithmic_bytes(Ts, na, Rs)["layer"]
-        sweep.append({"tokens": Ts, "us_per_call": mss * 1e3, "tokens_per_s": Ts / (mss * 1e-3),
+        st = stage_times(L, fns, 3, flush)
+        sweep.append({"tokens": Ts, "skew": SKEW_BOOST if skewed else 0.0, "us_per_call": mss * 1e3,
+                      "tokens_per_s": Ts / (mss * 1e-3),
                       "active_experts": na, "assignments": Rs, "hbm_gbs": bb / (mss * 1e-3) / 1e9,
                       "hbm_frac": bb / (mss * 1e-3) / 1e9 / hbm_peak,
-                      "fp8_tflops": Rs * FLOPS_PER_ASSIGNMENT / (mss * 1e-3) / 1e12})
+                      "fp8_tflops": Rs * FLOPS_PER_ASSIGNMENT / (mss * 1e-3) / 1e12,
+                      "stage_us": {k: round(v * 1e3, 1) for k, v in st.items()}})
+    skew_base = None
 
     clk.__exit__(None, None, None)
     clocks = clk.summary()
     clocks["window"] = "headline + sweep timed regions"
 
     cpu = None
-    if rank == 0 and not a.no_cpu_baseline:
+    if not a.no_cpu_baseline:
         sec, n, cores = cpu_baseline(inp, a.cpu_sample_s)
         cpu = {"value": T / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
                "sample": f"{n} full layer call(s) at T={T}, E_l={E_l} (fp32 oracle port, {sec:.2f} s/call)"}
@@ -550,11 +571,11 @@ def main():
                 "algorithmic_bytes": ab[dom], "kernel_ms": stages[dom],
                 "traffic": traffic_from_profile(workload, dom)}
     line = {
-        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": world,
+        "metric": "moe_layer_tokens_per_s", "value": value, "unit": "tokens/s", "n_gpus": 1,
         "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp8e4m3 (fp32 accumulate)", "data": "synthetic",
         "config": {"workload": workload, "tokens": T, "local_experts": E_l, "hidden": H, "intermediate": I,
-                   "experts": 256, "top_k": 8, "parallelism": "replicas" if world > 1 else "single",
+                   "experts": 256, "top_k": 8, "parallelism": "single",
                    "l2": "flushed (256 MiB write) before every timed step",
                    "active_experts": n_act, "assignments": R,
                    "layer_hbm_gbs": ab["layer"] / (ms * 1e-3) / 1e9,
@@ -564,16 +585,12 @@ def main():
         "stage_ms": stages,
         "sweep": sweep,
         "cpu_baseline": cpu,
-        "e2e": {"value": T * world / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
         "clocks": clocks,
         "gpu_launches": a.steps * L.load().moe_fp8_ds_launches_per_call(T),
     }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        torch.distributed.barrier()
-        torch.distributed.destroy_process_group()
+    print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":

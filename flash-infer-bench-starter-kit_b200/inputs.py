@@ -158,6 +158,22 @@ ARG_ORDER = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_s
              "local_expert_offset", "routed_scaling_factor")
 
 
+def bench_batch(T_base: int, skew: float = 0.0, device: str | torch.device = "cuda"):
+    """The benchmark's synthetic batch: ``T_base`` tokens and 32 local experts
+    (offset 0) drawn from seed 0 on ``device``; ``skew`` > 0 gives the skewed
+    stress batch (logits of experts 0-7 and 32-39 raised by ``skew``)."""
+    return make_inputs(T_base, E_l=32, local_expert_offset=0, seed=0, device=device, skew=skew)
+
+
+def token_slice(base: dict, T: int) -> dict:
+    """The first ``T`` tokens of a batch (weights shared)."""
+    d = dict(base)
+    d["routing_logits"] = base["routing_logits"][:T].contiguous()
+    d["hidden_states"] = base["hidden_states"][:T].contiguous()
+    d["hidden_states_scale"] = base["hidden_states_scale"][:, :T].contiguous()
+    return d
+
+
 def as_args(inp: dict):
     """The positional argument tuple of ``kernel(...)`` (without ``output``)."""
     return tuple(inp[k] for k in ARG_ORDER)

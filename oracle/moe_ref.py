@@ -70,19 +70,32 @@ def fp8_to_f32(x: torch.Tensor) -> torch.Tensor:
 # --------------------------------------------------------------------------
 # Routing (flashinfer moe.py:140-170; moe.cu:178-206)
 # --------------------------------------------------------------------------
+def exp_correctly_rounded(x: torch.Tensor) -> torch.Tensor:
+    """fp32 exp rounded once from a float64 evaluation (correct rounding except in
+    cases closer to a rounding boundary than float64's own error, none of which
+    occur in the tests' inputs)."""
+    return torch.exp(x.to(torch.float64)).to(torch.float32)
+
+
 def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
-          routed_scaling_factor: float):
+          routed_scaling_factor: float, exp=torch.exp):
     """DeepSeek-V3 no-aux routing.
 
     Returns ``(topk_idx int64 [T,8], topk_w fp32 [T,8], dense_w fp32 [T,256])``.
     ``topk_idx`` is sorted ascending per token (the reference's top-k is
     unsorted, so only the set is defined); ``topk_w[t,k]`` is the weight of
     expert ``topk_idx[t,k]``.
+
+    ``exp`` is the definition's ``torch.exp`` on CPU by default.  That function
+    is not correctly rounded (on an MKL build of torch it is MKL's ``vsExp``,
+    about 1% of results one ulp away from the correctly rounded value), so
+    ``exp=exp_correctly_rounded`` gives the same definition with a correctly
+    rounded exponential, which is what the CUDA routing computes.
     """
     T = routing_logits.shape[0]
     logits = routing_logits.to(torch.float32)
     bias = routing_bias.to(torch.float32).reshape(-1)
-    s = 1.0 / (1.0 + torch.exp(-logits))
+    s = 1.0 / (1.0 + exp(-logits))
     s_with_bias = s + bias
     gsz = E_GLOBAL // N_GROUP
     top2 = torch.topk(s_with_bias.view(T, N_GROUP, gsz), k=2, dim=2, sorted=False).values
@@ -109,7 +122,7 @@ def _route_weights(s: torch.Tensor, topk_idx: torch.Tensor, routed_scaling_facto
 
 
 def route_lowest_id_ties(routing_logits: torch.Tensor, routing_bias: torch.Tensor,
-                         routed_scaling_factor: float):
+                         routed_scaling_factor: float, exp=torch.exp):
     """``route`` with ties resolved as the reference's CUDA routing kernel does.
 
     ``torch.topk`` leaves the order of equal scores unspecified, so on inputs
@@ -123,7 +136,7 @@ def route_lowest_id_ties(routing_logits: torch.Tensor, routing_bias: torch.Tenso
     T = routing_logits.shape[0]
     logits = routing_logits.to(torch.float32)
     bias = routing_bias.to(torch.float32).reshape(-1)
-    s = 1.0 / (1.0 + torch.exp(-logits))
+    s = 1.0 / (1.0 + exp(-logits))
     s_with_bias = s + bias
     gsz = E_GLOBAL // N_GROUP
     top2 = torch.topk(s_with_bias.view(T, N_GROUP, gsz), k=2, dim=2, sorted=True).values

@@ -2,9 +2,12 @@
 and the reference's golden vectors.
 
 Tolerances (north star of the build): expert ids bit-exact; routing weights
-within 1 fp32 ulp (>= 99.9% of picks; the rest within 4 ulp, caused by torch's
-CPU exp not being correctly rounded); bf16 output within atol 1e-2 / rtol 2e-2
-of the fp32-intermediate reference.  Intermediate stages are checked tighter,
+bit-exact against the definition evaluated with a correctly rounded exp (the
+definition's own CPU ``torch.exp`` is MKL's vsExp, one ulp off correct rounding
+for ~1% of inputs, which moves ~0.2% of its weights by 1-3 ulp: the GPU weights
+are compared with the golden weights too and must sit exactly as close to them
+as the correctly rounded definition does); bf16 output within atol 1e-2 / rtol
+2e-2 of the fp32-intermediate reference.  Intermediate stages are checked tighter,
 against the oracle fed with the GPU's own upstream result.
 """
 
@@ -82,7 +85,7 @@ def check_output(got_bf16, ref_fp32):
 
 # ---------------------------------------------------------------------------- routing
 @pytest.mark.parametrize("name", ["route_T4096_s3", "route_T2048_skew_s4"])
-def test_routing_matches_reference(name, pkg, cuda_dev):
+def test_routing_matches_reference(name, pkg, oracle, cuda_dev):
     g = load_golden(name)
     logits, bias = pkg.inputs.make_routing_inputs(g["T"], seed=g["seed"], skew=g["skew"])
     T = g["T"]
@@ -99,10 +102,12 @@ def test_routing_matches_reference(name, pkg, cuda_dev):
     L.check(st, "moe_fp8_ds_route")
     torch.cuda.synchronize()
     assert torch.equal(ids.cpu(), g["topk_ids"]), "expert ids differ from the reference"
+    _, w_cr, _ = oracle.route(logits, bias, 2.5, exp=oracle.exp_correctly_rounded)
+    assert torch.equal(w.cpu(), w_cr), "weights differ from the correctly rounded definition"
     u = ulp_distance(w.cpu(), g["topk_w"])
-    frac1 = float((u <= 1).float().mean())
-    print(f"{name}: weights ulp hist {[int((u == k).sum()) for k in range(5)]} max {int(u.max())}")
-    assert frac1 >= 0.999 and int(u.max()) <= 4
+    u_def = ulp_distance(w_cr, g["topk_w"])
+    print(f"{name}: weights vs golden ulp hist {[int((u == k).sum()) for k in range(5)]} max {int(u.max())}")
+    assert torch.equal(u, u_def)
 
 
 @pytest.mark.parametrize("T,seed,bias_grid", [(512, 0, False), (300, 1, True)])
@@ -123,10 +128,9 @@ def test_routing_ties_break_toward_lowest_id(T, seed, bias_grid, pkg, oracle, cu
                                    ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     L.check(st, "moe_fp8_ds_route")
     torch.cuda.synchronize()
-    want_ids, want_w, _ = oracle.route_lowest_id_ties(logits, bias, 2.5)
+    want_ids, want_w, _ = oracle.route_lowest_id_ties(logits, bias, 2.5, exp=oracle.exp_correctly_rounded)
     assert torch.equal(ids.cpu(), want_ids.to(torch.int32)), "tie-breaking differs from the reference kernel"
-    u = ulp_distance(w.cpu(), want_w)
-    assert int(u.max()) <= 4 and float((u <= 1).float().mean()) >= 0.999
+    assert torch.equal(w.cpu(), want_w)
 
 
 # ---------------------------------------------------------------------------- golden
@@ -169,15 +173,47 @@ STAGE_CASES = [
 def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
     inp = cached_inputs(T, E_l, off, seed, skew)
     path = bn[2] if len(bn) > 2 else 0
-    out, ws, lay = run_layer(pkg, to_dev(inp, cuda_dev), bn=bn[:2], path=path)
+    check_stages(pkg, oracle, inp, to_dev(inp, cuda_dev), bn[:2], path)
+
+
+# The benchmark's own batches: ``inputs.bench_batch`` draws them on the GPU from
+# seed 0 (decode and prefill points are the first T tokens of one 4096-token
+# batch; the skewed stress point is its own 16384-token batch with experts 0-7
+# and 32-39 hot).  ``experts`` limits the per-expert GEMM stage checks (the
+# CPU oracle's cost grows with the rows per expert); routing, permutation and
+# the whole output are always checked.
+BENCH_CASES = [
+    # T_base, T, skew, experts checked stage by stage
+    (4096, 1024, 0.0, None),
+    (4096, 4096, 0.0, None),
+    (16384, 16384, 3.0, (0, 3, 7, 8, 20, 31)),
+]
+
+
+@pytest.mark.parametrize("T_base,T,skew,experts", BENCH_CASES)
+def test_benchmark_shapes(T_base, T, skew, experts, pkg, oracle, cuda_dev):
+    dev_inp = pkg.inputs.token_slice(pkg.inputs.bench_batch(T_base, skew=skew, device=cuda_dev), T)
+    inp = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in dev_inp.items()}
+    check_stages(pkg, oracle, inp, dev_inp, (0, 0), 0, experts=experts)
+
+
+def check_stages(pkg, oracle, inp, inp_dev, bn, path, experts=None):
+    """Run the layer on ``inp_dev`` and check every stage against the oracle fed
+    the GPU's upstream result: routing and permutation bit-exact, GEMM1+SwiGLU
+    and GEMM2 per expert, then the whole output."""
+    T = inp["hidden_states"].shape[0]
+    E_l = inp["gemm1_weights"].shape[0]
+    off = inp["local_expert_offset"]
+    out, ws, lay = run_layer(pkg, inp_dev, bn=bn, path=path)
     wide = path >= 2 or (path == 0 and T >= 1536)
     R = lay.row_capacity
     # routing
-    ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"],
+                                     exp=oracle.exp_correctly_rounded)
     ids = ws_view(ws, lay.topk_ids, T * 8, torch.int32).view(T, 8).cpu()
     w = ws_view(ws, lay.topk_weights, T * 8, torch.float32).view(T, 8).cpu()
     assert torch.equal(ids, ids_ref.to(torch.int32))
-    assert int(ulp_distance(w, w_ref).max()) <= 4
+    assert torch.equal(w, w_ref)
     # permutation
     seg_ref, row_tok_ref, _, inv_ref = oracle.local_assignments(ids_ref, off, E_l)
     seg = ws_view(ws, lay.seg_offsets, E_l + 1, torch.int32).cpu().long()
@@ -207,7 +243,7 @@ def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
         assert torch.equal(act16, A[row_tok].to(torch.float16))
         deq = ws_view(ws, lay.inter16, R * 2048, torch.float16).view(R, 2048)[:nrows].cpu().float()
         g1_tol, g2_tol = 3e-3, 2e-3            # f16 operands: 2^-12 relative per element
-    for e in range(E_l):
+    for e in (range(E_l) if experts is None else experts):
         r0, r1 = int(seg[e]), int(seg[e + 1])
         if r0 == r1:
             continue
@@ -224,7 +260,9 @@ def test_layer_stages(T, E_l, off, seed, skew, bn, pkg, oracle, cuda_dev):
         assert bool((d <= tol).all()), f"expert {e}: GEMM2 mismatch {float(d.max()):.3e}"
     ref32 = oracle.moe_forward(*pkg.inputs.as_args(inp), return_fp32=True)
     mx, mr = check_output(out, ref32)
-    print(f"T={T} E_l={E_l} bn={bn}: rows {nrows} max_abs {mx:.3e} mean_rel {mr:.3e}")
+    counts = (seg[1:] - seg[:-1]).tolist()
+    print(f"T={T} E_l={E_l} bn={bn} path={path}: rows {nrows} (per expert {min(counts)}..{max(counts)}) "
+          f"max_abs {mx:.3e} mean_rel {mr:.3e}")
 
 
 # ---------------------------------------------------------------------------- contract
