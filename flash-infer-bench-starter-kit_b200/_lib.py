@@ -62,6 +62,7 @@ EXPORTS = (
     "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc", "moe_fp8_ds_set_path_override",
     "moe_fp8_ds_ep_plan", "moe_fp8_ds_ep_pack", "moe_fp8_ds_ep_unpack", "moe_fp8_ds_ep_combine",
     "moe_fp8_ds_selftest_wait_timeout", "moe_fp8_ds_noalloc_read_device_error",
+    "moe_fp8_ds_last_cuda_error_string",
 )
 
 _lib = None
@@ -96,6 +97,8 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_read_device_error.argtypes = [P, P, ctypes.POINTER(I32)]
         lib.moe_fp8_ds_status_string.argtypes = [ctypes.c_int]
         lib.moe_fp8_ds_status_string.restype = ctypes.c_char_p
+        lib.moe_fp8_ds_last_cuda_error_string.argtypes = []
+        lib.moe_fp8_ds_last_cuda_error_string.restype = ctypes.c_char_p
         lib.moe_fp8_ds_launches_per_call.argtypes = [I32]
         lib.moe_fp8_ds_set_tile_override.argtypes = [I32, I32]
         lib.moe_fp8_ds_set_stage_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), I32]
@@ -105,7 +108,7 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_ep_combine.argtypes = [P, P, I32, I32, P, P]
         lib.moe_fp8_ds_selftest_wait_timeout.argtypes = [P, P]
         for name in EXPORTS:
-            if name != "moe_fp8_ds_status_string":
+            if name not in ("moe_fp8_ds_status_string", "moe_fp8_ds_last_cuda_error_string"):
                 getattr(lib, name).restype = ctypes.c_int
         _lib = lib
         return lib
@@ -120,4 +123,6 @@ def status_string(status: int) -> str:
 
 def check(status: int, where: str) -> None:
     if status != MOE_OK:
+        if status == MOE_ERR_CUDA:
+            where = f"{where} ({load().moe_fp8_ds_last_cuda_error_string().decode()})"
         raise MoeError(status, where)

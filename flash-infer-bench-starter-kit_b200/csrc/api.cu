@@ -29,10 +29,19 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
-int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs
-constexpr int kWideMinTokens = 1536;
+int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs, 3 tokens-on-M e4m3
+// From this batch size the layer runs the tokens-on-M e4m3 GEMMs (gemm_tm.cu).
+constexpr int kTmMinTokens = 512;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
+
+// The CUDA error behind the calling thread's last MOE_ERR_CUDA.
+thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = e;
+  return MOE_ERR_CUDA;
+}
 
 void mark_stage(int i, cudaStream_t s) {
   if (g_stage_events_on) cudaEventRecord(g_stage_events[i], s);
@@ -76,7 +85,8 @@ struct Plan {
   moe_fp8_ds_layout pub;
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
   int bt1, bt2;                     // compiled tile width of each GEMM (>= bn: the tile cap)
-  bool wide;                        // large batch: f16-operand GEMMs (gemm_f16.cu)
+  bool wide;                        // f16-operand GEMMs (gemm_f16.cu), on request only
+  bool tm;                          // large batch: tokens-on-M e4m3 GEMMs (gemm_tm.cu)
   uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2, front_sync;
 };
 
@@ -95,16 +105,22 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->T = T;
   P->E_l = E_l;
   P->NB = (T + kPermBlock - 1) / kPermBlock;
-  P->R_cap = T * (E_l < kTopK ? E_l : kTopK);
+  // row capacity, a multiple of 16 so that per-row fp32 arrays [blocks][R_cap]
+  // have 16-byte-aligned rows (TMA boxes of the tokens-on-M GEMMs)
+  P->R_cap = (T * (E_l < kTopK ? E_l : kTopK) + 15) & ~15;
   // GEMM1 keeps X1 and X2 accumulators of 128 features per token column in
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  // f16-operand GEMMs win once experts see ~48+ tokens each (measured on B200
-  // with 32 local experts, layer time e4m3 / f16: T=1024 381/414 us, 1536
-  // 470/470, 2048 562/500, 3072 758/644, 16384 3047/2190).
-  P->wide = path_override >= 2 || (path_override == 0 && T >= kWideMinTokens);
-  if (P->wide) {
+  P->wide = path_override == 2;
+  P->tm = path_override == 3 || (path_override == 0 && T >= kTmMinTokens);
+  if (P->tm) {
+    // One token tile holds up to 128 rows of one expert (the MMA's M side); a
+    // smaller tile cap may be forced for tests.
+    auto cap = [](int v) { return v > 0 && v <= 128 ? v : 128; };
+    P->bn1 = P->bn2 = cap(bn_override[0]);
+    P->bt1 = P->bt2 = 128;
+  } else if (P->wide) {
     // f16 kernels accumulate in TMEM, so one tile takes up to 256 tokens.
     // The widest tiles win, measured on B200 with 32 local experts: each
     // weight byte a CTA converts then serves the most tokens, and full-height
@@ -157,6 +173,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->ready = take((uint64_t)E_l * 4);
   P->pub.row_token = take(R * 4);
   const uint64_t R8 = P->wide ? 0 : R, R16 = P->wide ? R : 0;   // only the active path's buffers
+  // (the tokens-on-M GEMMs use the e4m3 buffers; their intermediate holds the
+  // hi and lo planes [2][R_cap][2048] in the same bytes as the row pairs)
   P->pub.act = take(R8 * kHidden);
   P->pub.act_scale = take(R8 * kHiddenBlocks * 4);
   P->pub.inter = take(2 * R8 * kInter);
@@ -164,7 +182,11 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->pub.act16 = take(R16 * kHidden * 2);
   P->pub.inter16 = take(R16 * kInter * 2);
   P->pub.down = take(R * kHidden * 4);
-  if (P->wide) {
+  if (P->tm) {
+    P->grid1 = P->grid2 = sm_count;
+    P->partials1 = take(gemm_tm_partials_bytes(P->grid1));
+    P->partials2 = take(gemm_tm_partials_bytes(P->grid2));
+  } else if (P->wide) {
     P->grid1 = P->grid2 = sm_count;
     P->partials1 = take(gemm_f16_partials_bytes(1, P->bt1, P->grid1));
     P->partials2 = take(gemm_f16_partials_bytes(2, P->bt2, P->grid2));
@@ -215,6 +237,30 @@ bool encode_b16_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t row
   return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
                   estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// fp32 [rows][cols] row-major (cols * 4 a multiple of 16 bytes); box = box_cols x box_rows.
+bool encode_f32_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
+                   uint32_t box_rows) {
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {cols * 4};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// fp32 [d2][d1][d0] row-major; box = b0 x b1 x b2.
+bool encode_f32_3d(CUtensorMap* m, const void* base, uint64_t d0, uint64_t d1, uint64_t d2, uint32_t b0,
+                   uint32_t b1, uint32_t b2) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {d0 * 4, d0 * d1 * 4};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
@@ -279,11 +325,31 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   __half* act16 = reinterpret_cast<__half*>(at(P.pub.act16));
   __half* inter16 = reinterpret_cast<__half*>(at(P.pub.inter16));
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
+  CUtensorMap tm_bs1, tm_ws1, tm_bs2, tm_ws2;   // tokens-on-M GEMMs: block scales
   if (P.wide) {
     if (!encode_w8_atoms(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out) ||
         !encode_b16_atoms(&tm_b1, act16, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
         !encode_w8_atoms(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden) ||
         !encode_b16_atoms(&tm_b2, inter16, kInter, (uint64_t)P.R_cap, (uint32_t)P.bn2))
+      return MOE_ERR_INVALID_ARGUMENT;
+  } else if (P.tm) {
+    // tokens-on-M GEMMs: 128-row boxes of tokens (GEMM2: hi plane rows r, lo
+    // plane rows R_cap + r) and of weights
+    const uint32_t ks1 = (uint32_t)gemm_tm_k_per_stage(1), ks2 = (uint32_t)gemm_tm_k_per_stage(2);
+    if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
+        !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, 128, ks1) ||
+        !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
+        !encode_kmajor(&tm_b2, inter, kInter, 2ull * P.R_cap, 128, ks2))
+      return MOE_ERR_INVALID_ARGUMENT;
+    // token scales [K blocks][R_cap]: boxes of 132 rows x the stage's K blocks;
+    // weight scales: 4 K blocks of each half's 128-row block
+    const uint32_t sbox = (uint32_t)gemm_tm_scale_box_cols();
+    if (!aligned16(a->gemm1_weights_scale) || !aligned16(a->gemm2_weights_scale))
+      return MOE_ERR_MISALIGNED;
+    if (!encode_f32_2d(&tm_bs1, act_scale, (uint64_t)P.R_cap, kHiddenBlocks, sbox, ks1) ||
+        !encode_f32_2d(&tm_bs2, inter_scale, (uint64_t)P.R_cap, kInterBlocks, sbox, ks2) ||
+        !encode_f32_3d(&tm_ws1, a->gemm1_weights_scale, kHiddenBlocks, kInter / 128, 2ull * E_l, 4, 1, 2) ||
+        !encode_f32_3d(&tm_ws2, a->gemm2_weights_scale, kInterBlocks, kHidden / 128, (uint64_t)E_l, 4, 2, 1))
       return MOE_ERR_INVALID_ARGUMENT;
   } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
@@ -295,7 +361,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   }
 
   cudaError_t ce;
-  const bool front = !routed && T <= kFrontMaxTokens && !P.wide;
+  const bool front = !routed && T <= kFrontMaxTokens && !P.wide && !P.tm;
   if (front) {
     // Small batch: routing, row assignment and gather in one launch.
     mark_stage(0, s);
@@ -304,57 +370,60 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
                       a->hidden_states, a->hidden_states_scale, ids, wts, masks8, P.NB8, seg, tiles1, tiles2,
                       sched, cnt1, cnt2, ready, inv, row_token, act, act_scale, err,
                       reinterpret_cast<int*>(at(P.front_sync)), s);
-    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    if (ce != cudaSuccess) return cuda_fail(ce);
     mark_stage(1, s);
     mark_stage(2, s);
   } else {
     mark_stage(0, s);
     ce = launch_route(routed, a->routing_logits, a->routing_bias, T, a->routed_scaling_factor,
                       a->local_expert_offset, E_l, ids, wts, masks8, P.NB8, err, s);
-    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    if (ce != cudaSuccess) return cuda_fail(ce);
     mark_stage(1, s);
     ce = launch_scan(masks8, P.NB8, bases, P.NB, E_l, seg, P.bn1, P.bn2, tiles1, tiles2, sched, cnt1,
-                     kInter / 128, cnt2, kHidden / 128, ready, s);
-    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+                     P.tm ? gemm_tm_units_per_tile(1) : kInter / 128, cnt2,
+                     P.tm ? gemm_tm_units_per_tile(2) : kHidden / 128, ready, s);
+    if (ce != cudaSuccess) return cuda_fail(ce);
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
                         a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale,
                         P.wide ? act16 : nullptr, s);
-    if (ce != cudaSuccess) return MOE_ERR_CUDA;
+    if (ce != cudaSuccess) return cuda_fail(ce);
   }
 
   GemmParams g1{};
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
   g1.b_scale = act_scale;
   g1.counters = cnt1; g1.ready = ready; g1.seg = seg; g1.bn_prev = 0;
-  g1.early_start = (!routed && T <= kFrontMaxTokens && !P.wide) ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
+  g1.early_start = front ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
   g1.inter16 = inter16;
   g1.box_rows = P.bn1;
   g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
   g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
-  ce = P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
-              : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  ce = P.tm     ? launch_gemm_tm(1, &tm_w1, &tm_b1, &tm_bs1, &tm_ws1, g1, P.grid1, s)
+       : P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
+                : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
+  if (ce != cudaSuccess) return cuda_fail(ce);
 
   GemmParams g2{};
   g2.tiles = tiles2; g2.sched = sched; g2.w_scale = a->gemm2_weights_scale;
   g2.b_scale = inter_scale;
   g2.counters = cnt2; g2.ready = ready; g2.seg = seg; g2.bn_prev = P.bn1;
-  g2.early_start = (!routed && T <= kFrontMaxTokens && !P.wide) ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
+  g2.early_start = front ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
   g2.inter16 = nullptr;
   g2.box_rows = P.bn2;
-  ce = P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
-              : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  ce = P.tm     ? launch_gemm_tm(2, &tm_w2, &tm_b2, &tm_bs2, &tm_ws2, g2, P.grid2, s)
+       : P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
+                : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
+  if (ce != cudaSuccess) return cuda_fail(ce);
 
   mark_stage(5, s);
   ce = launch_combine(down, inv, wts, T, a->output, a->output_f32,
                       front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr, err, s);
-  if (ce != cudaSuccess) return MOE_ERR_CUDA;
+  if (ce != cudaSuccess) return cuda_fail(ce);
   mark_stage(6, s);
   return MOE_OK;
 }
@@ -465,6 +534,10 @@ int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t* device_
   return MOE_ERR_DEVICE_FAULT;
 }
 
+const char* moe_fp8_ds_last_cuda_error_string(void) {
+  return cudaGetErrorString(g_last_cuda_error);
+}
+
 const char* moe_fp8_ds_status_string(int status) {
   switch (status) {
     case MOE_OK: return "ok";
@@ -502,7 +575,7 @@ int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
 }
 
 int moe_fp8_ds_set_path_override(int32_t mode) {
-  if (mode < 0 || mode > 2) return MOE_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 3) return MOE_ERR_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lk(g_mu);
   g_path_override = mode;
   return MOE_OK;

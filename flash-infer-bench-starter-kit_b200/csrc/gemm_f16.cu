@@ -295,7 +295,7 @@ moe_gemm_f16_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_const
       const int mt = mn.x, nt = mn.y;
       const int4 tile = p.tiles[mt];
       const int b = seg % C::NACC;
-      const bool got = mbar_wait_bounded(&accf[b], (seg / C::NACC) & 1, abort_flag);
+      const bool got = mbar_wait_warp(&accf[b], (seg / C::NACC) & 1, abort_flag);
       if (named_bar_or(1, 128, !got || *abort_flag != 0)) break;
       tc_fence_after();
       const uint32_t acc0 = tmem_base + lane_addr + (uint32_t)(b * C::ACC);

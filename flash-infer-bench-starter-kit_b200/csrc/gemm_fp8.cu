@@ -298,7 +298,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       }
       const float pre = (loader && i + 2 < n_iter) ? fetch(i + 2) : 0.f;
       const float* sl = sring + (i % C::RING) * C::SLOT;
-      const bool got = mbar_wait_bounded(&tfull[b], (i / C::NBUF) & 1, abort_flag);
+      const bool got = mbar_wait_warp(&tfull[b], (i / C::NBUF) & 1, abort_flag);
       if (got) {
         tc_fence_after();
 #pragma unroll

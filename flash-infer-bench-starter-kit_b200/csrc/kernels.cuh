@@ -24,7 +24,7 @@ struct GemmParams {
   int front_ctas;
   int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
-  uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048]
+  uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048] (row pairs, or hi/lo planes)
   float* inter_scale;         // GEMM1 output: [16, R_cap]
   float* down;                // GEMM2 output: fp32 [R_cap, 7168]
   __half* inter16;            // f16 GEMM1 output (large batches): [R_cap, 2048]
@@ -98,7 +98,15 @@ int gemm_ctas_per_sm(int kind, int bn);
 cudaError_t launch_gemm(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                         const GemmParams& p, int grid, cudaStream_t st);
 
-// f16-operand GEMMs for large batches (gemm_f16.cu).
+// e4m3 GEMMs with tokens on the MMA's M side, for large batches (gemm_tm.cu).
+size_t gemm_tm_partials_bytes(int grid);
+int gemm_tm_k_per_stage(int kind);
+int gemm_tm_units_per_tile(int kind);
+int gemm_tm_scale_box_cols();
+cudaError_t launch_gemm_tm(int kind, const CUtensorMap* tm_w, const CUtensorMap* tm_b, const CUtensorMap* tm_bs,
+                           const CUtensorMap* tm_ws, const GemmParams& p, int grid, cudaStream_t st);
+
+// f16-operand GEMMs (gemm_f16.cu).
 size_t gemm_f16_partials_bytes(int kind, int bn, int grid);
 cudaError_t launch_gemm_f16(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
                              const GemmParams& p, int grid, cudaStream_t st);

@@ -165,19 +165,27 @@ MOE_API int moe_fp8_ds_read_device_error(void* workspace, void* stream, int32_t*
  * context stays usable.  Uses 16 bytes at the workspace base.              */
 MOE_API int moe_fp8_ds_selftest_wait_timeout(void* workspace, void* stream);
 
+/* Description of the CUDA runtime error behind the calling thread's last
+ * MOE_ERR_CUDA from a layer call (a launch or attribute failure); "no error"
+ * if there was none.  No counterpart in the reference.                     */
+MOE_API const char* moe_fp8_ds_last_cuda_error_string(void);
+
 /* Static description of a status code. */
 MOE_API const char* moe_fp8_ds_status_string(int status);
 
 /* Tuning knob: force the token-tile cap (a multiple of 16, at most 256) of
  * GEMM1 and GEMM2 for calls on this process; 0 restores the automatic choice
- * from T.  The e4m3 GEMMs take 16, 32, 64 or 128 and use the automatic choice
- * for other values; the f16 GEMMs take any.  Takes effect for the next call
- * (workspace size included). */
+ * from T.  The weights-on-M e4m3 GEMMs take 16, 32, 64 or 128 and use the
+ * automatic choice for other values; the f16 GEMMs take any; the tokens-on-M
+ * GEMMs take the GEMM1 value (at most 128) for both.  Takes effect for the
+ * next call (workspace size included). */
 MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
-/* Tuning knob: 0 = automatic GEMM family (e4m3 block-promotion GEMMs for
- * T < 1536, f16-operand TMEM-accumulating GEMMs from 1536 tokens), 1 = always
- * e4m3, 2 = always f16.  Takes effect for the next call (workspace size
+/* Tuning knob: 0 = automatic GEMM family (e4m3 GEMMs with weights on the
+ * MMA's M side for T < 512, e4m3 GEMMs with tokens on M from 512 tokens),
+ * 1 = always weights-on-M e4m3, 2 = always f16-operand GEMMs (block scales
+ * folded into f16 operands; never chosen automatically), 3 = always
+ * tokens-on-M e4m3.  Takes effect for the next call (workspace size
  * included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);
 
