@@ -239,6 +239,22 @@ bool encode_b16_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t row
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// K-major e4m3 operand in two planes, viewed as {128 B of a K block, row, K
+// block, plane}: W13 [E_l][2][2048][7168] (plane = expert*2 + X1|X2) or the
+// intermediate [2][R_cap][2048] (plane = hi|lo).  A box covers box_rows rows
+// x kblocks K blocks x 2 planes, landing as [plane][K block][row][128 B]
+// with 128-byte swizzling.
+bool encode_kmajor_planes(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint64_t planes,
+                          uint32_t box_rows, uint32_t kblocks) {
+  cuuint64_t dims[4] = {128, rows, K / 128, planes};
+  cuuint64_t strides[3] = {K, 128, rows * K};
+  cuuint32_t box[4] = {128, box_rows, kblocks, 2};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // fp32 [rows][cols] row-major (cols * 4 a multiple of 16 bytes); box = box_cols x box_rows.
 bool encode_f32_2d(CUtensorMap* m, const void* base, uint64_t cols, uint64_t rows, uint32_t box_cols,
                    uint32_t box_rows) {
@@ -336,10 +352,10 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     // tokens-on-M GEMMs: 128-row boxes of tokens (GEMM2: hi plane rows r, lo
     // plane rows R_cap + r) and of weights
     const uint32_t ks1 = (uint32_t)gemm_tm_k_per_stage(1), ks2 = (uint32_t)gemm_tm_k_per_stage(2);
-    if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
+    if (!encode_kmajor_planes(&tm_w1, a->gemm1_weights, kHidden, kInter, 2ull * E_l, 128, ks1) ||
         !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, 128, ks1) ||
-        !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
-        !encode_kmajor(&tm_b2, inter, kInter, 2ull * P.R_cap, 128, ks2))
+        !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 256, ks2) ||
+        !encode_kmajor_planes(&tm_b2, inter, kInter, (uint64_t)P.R_cap, 2, 128, ks2))
       return MOE_ERR_INVALID_ARGUMENT;
     // token scales [K blocks][R_cap]: boxes of 132 rows x the stage's K blocks;
     // weight scales: 4 K blocks of each half's 128-row block

@@ -150,12 +150,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Wait until the phase with the given parity has completed.  Gives up (and
 // sets *abort) after kWaitLimitNs, or as soon as another role has aborted.
+// The clock and the abort flag are checked once per 64 polls: reading
+// %globaltimer between polls delayed the wake-up after a phase completed by
+// up to a microsecond on B200.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   volatile int* abort_flag) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int k = 0; k < 64; ++k)
+      if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer_ns() - t0 > kWaitLimitNs) {
       *abort_flag = 1;
@@ -198,6 +203,16 @@ __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* ba
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+// 4D tiled load (coordinates innermost first).
+__device__ __forceinline__ void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,
+                                            int32_t x, int32_t y, int32_t z, int32_t w, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], %7;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "r"(w), "l"(policy)
       : "memory");
 }
 

@@ -63,18 +63,23 @@ struct TmCfg {
   static constexpr int W_PROD = 8, W_MMA = 9;               // producer and MMA warps
   static constexpr int THREADS = NEPI + 64;
   static constexpr int COLS = 64;                           // columns of each half per epilogue thread
-  // Block scales travel with their stage: KS rows of 132 fp32 token scales
-  // (a TMA box starting at the tile's first row rounded down to a multiple of
-  // 4, so its x coordinate is 16-byte aligned) and the two halves' weight
-  // scales (a box of 4 K blocks per half, likewise aligned).
+  // Block scales travel in their own ring of SR slots, one per pipeline
+  // iteration: KS rows of 132 fp32 token scales (a TMA box starting at the
+  // tile's first row rounded down to a multiple of 4, so its x coordinate is
+  // 16-byte aligned) and the two halves' weight scales (a box of 4 K blocks
+  // per half, likewise aligned).  A separate, deeper ring lets an operand
+  // stage be refilled as soon as its MMAs are done, however far the epilogue
+  // lags behind the tensor core.
+  static constexpr int SR = 8;
   static constexpr int SC_ROW = 132;
   static constexpr int SC_ACT = KS * SC_ROW * 4;
   static constexpr int SC_SLOT = ((SC_ACT + 127) / 128) * 128 + 128;
   static constexpr int SC_TX = SC_ACT + 2 * 4 * 4;
   static constexpr int OFF_SC = 2048 + 2 * 2 * 128 * 4;    // after barriers + amax exchange [2][2][128]
-  static constexpr int AUX = OFF_SC + STAGES * SC_SLOT;
+  static constexpr int AUX = OFF_SC + SR * SC_SLOT;
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
   static_assert(KS == 1 || KS == 2 || KS == 4, "weight-scale boxes cover 4 aligned K blocks");
+  static_assert(KIND == 1 || KS == 1, "GEMM2's 256-row weight box holds one K block");
   static constexpr uint32_t SLOT_COLS = 256, P_B = 128;     // partial slot: half A at +0, half B at +128
   static constexpr int PART_FLOATS = 128 * 256;             // one published share: [128 rows][256 cols]
   static_assert(KB % KS == 0, "K steps");
@@ -94,12 +99,14 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
   uint64_t* empty = full + STAGES;                          // MMAs finished reading stage s
   uint64_t* pfull = empty + STAGES;                         // [2] partial slot written
   uint64_t* pempty = pfull + 2;                             // [2] partial slot read
-  uint64_t* drain = pempty + 2;
+  uint64_t* sfull = pempty + 2;                             // [SR] scales of an iteration landed
+  uint64_t* sempty = sfull + C::SR;                         // [SR] scales read by every epilogue warp
+  uint64_t* drain = sempty + C::SR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = const_cast<int*>(abort_flag) + 1;
   float* s_amax = reinterpret_cast<float*>(aux + 2048);     // [2 buffers][2 warpgroups][128 rows]
-  uint8_t* s_sc = aux + C::OFF_SC;                          // [STAGES][SC_SLOT] scales per stage
+  uint8_t* s_sc = aux + C::OFF_SC;                          // [SR][SC_SLOT] scales per iteration
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -111,9 +118,8 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
   if (n_iter == 0) return;   // uniform: this CTA has no work
 
   if (threadIdx.x == 0) {
-    // a stage is free once its MMAs are done (one commit) and every epilogue
-    // warp has read its scales
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1 + C::NEPI / 32); }
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+    for (int s = 0; s < C::SR; ++s) { mbar_init(&sfull[s], 1); mbar_init(&sempty[s], C::NEPI / 32); }
     for (int h = 0; h < 2; ++h) { mbar_init(&pfull[h], 1); mbar_init(&pempty[h], C::NEPI / 32); }
     mbar_init(drain, 1);
     *const_cast<int*>(abort_flag) = 0;
@@ -136,7 +142,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     if (elect_one_lane()) {
       const uint64_t pol_w = l2_policy_evict_first();
       const uint64_t pol_b = l2_policy_evict_last();
-      int issued = 0;
+      int issued = 0, sissued = 0;
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
         int u, ks, r;
@@ -145,27 +151,43 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         const int4 tile = p.tiles[mn.x];
         const int s = i % STAGES;
         if (!mbar_wait_bounded(&empty[s], ((i / STAGES) & 1) ^ 1, abort_flag)) { ok = false; break; }
-        mbar_arrive_expect_tx(&full[s], C::STAGE + C::SC_TX);
+        mbar_arrive_expect_tx(&full[s], C::STAGE);
         uint8_t* st = smem + s * C::STAGE;
         const int z = ks * KS;
-        uint8_t* sc = s_sc + s * C::SC_SLOT;
-        tma_load_2d(&tm_bs, &full[s], sc, tile.y & ~3, z, pol_b);
-        if (KIND == 1)   // w_scale viewed as {56 K blocks, 16 n-blocks, 2 halves x E_l}
-          tma_load_3d(&tm_ws, &full[s], sc + C::SC_SLOT - 128, z & ~3, mn.y, 2 * tile.x, pol_b);
-        else             // w_scale viewed as {16 K blocks, 56 n-blocks, E_l}
-          tma_load_3d(&tm_ws, &full[s], sc + C::SC_SLOT - 128, z & ~3, 2 * mn.y, tile.x, pol_b);
-        tma_load_3d(&tm_b, &full[s], st, 0, tile.y, z, pol_b);
-        if (KIND == 2) tma_load_3d(&tm_b, &full[s], st + KS * C::TILE, 0, p.R_cap + tile.y, z, pol_b);
-        const int wrow = tile.x * C::W_ROWS + (KIND == 1 ? mn.y * 128 : mn.y * 256);
-        tma_load_3d(&tm_w, &full[s], st + C::OFF_WA, 0, wrow, z, pol_w);
-        tma_load_3d(&tm_w, &full[s], st + C::OFF_WB, 0, wrow + (KIND == 1 ? kInter : 128), z, pol_w);
+        // Two operand boxes per stage (fewer, larger TMA boxes stream faster):
+        // GEMM1 tokens {128 B, 128 rows, KS} + weights {128 B, 128 rows, KS,
+        // X1|X2} (W13 viewed as [2E_l][56][2048][128 B]); GEMM2 tokens {128 B,
+        // 128 rows, KS, hi|lo} + weights {128 B, 256 rows, KS}.
+        if (KIND == 1) {
+          tma_load_3d(&tm_b, &full[s], st, 0, tile.y, z, pol_b);
+          tma_load_4d(&tm_w, &full[s], st + C::OFF_WA, 0, mn.y * 128, z, 2 * tile.x, pol_w);
+        } else {
+          tma_load_4d(&tm_b, &full[s], st, 0, tile.y, z, 0, pol_b);
+          tma_load_3d(&tm_w, &full[s], st + C::OFF_WA, 0, tile.x * C::W_ROWS + mn.y * 256, z, pol_w);
+        }
         ++issued;
+        // this iteration's block scales into scale slot i % SR
+        const int q = i % C::SR;
+        if (!mbar_wait_bounded(&sempty[q], ((i / C::SR) & 1) ^ 1, abort_flag)) { ok = false; break; }
+        mbar_arrive_expect_tx(&sfull[q], C::SC_TX);
+        uint8_t* sc = s_sc + q * C::SC_SLOT;
+        tma_load_2d(&tm_bs, &sfull[q], sc, tile.y & ~3, z, pol_b);
+        if (KIND == 1)   // w_scale viewed as {56 K blocks, 16 n-blocks, 2 halves x E_l}
+          tma_load_3d(&tm_ws, &sfull[q], sc + C::SC_SLOT - 128, z & ~3, mn.y, 2 * tile.x, pol_b);
+        else             // w_scale viewed as {16 K blocks, 56 n-blocks, E_l}
+          tma_load_3d(&tm_ws, &sfull[q], sc + C::SC_SLOT - 128, z & ~3, 2 * mn.y, tile.x, pol_b);
+        ++sissued;
       }
       if (!ok) {
         raise_error(p.err, kDevTimeoutProducer);
         for (int i = max(0, issued - STAGES); i < issued; ++i) {   // let copies in flight land
           const unsigned long long t0 = globaltimer_ns();
           while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) &&
+                 globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
+        }
+        for (int i = max(0, sissued - C::SR); i < sissued; ++i) {
+          const unsigned long long t0 = globaltimer_ns();
+          while (!mbar_try_wait(&sfull[i % C::SR], (i / C::SR) & 1) &&
                  globaltimer_ns() - t0 < kWaitLimitNs / 10) {}
         }
       }
@@ -241,13 +263,13 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
 #pragma unroll
           for (int x = 0; x < C::COLS; ++x) acc[h][x] = 0.f;
       }
-      // this stage's scales: promotion coefficients of its K blocks
-      const int s = i % STAGES;
+      // this iteration's scales: promotion coefficients of its K blocks
+      const int sq = i % C::SR;
       float cA[KS], cB[KS];
-      if (!mbar_wait_warp(&full[s], (i / STAGES) & 1, abort_flag)) aborted = true;
+      if (!mbar_wait_warp(&sfull[sq], (i / C::SR) & 1, abort_flag)) aborted = true;
       if (!aborted) {
-        const float* sc = reinterpret_cast<const float*>(s_sc + s * C::SC_SLOT);
-        const float* wsc = reinterpret_cast<const float*>(s_sc + s * C::SC_SLOT + C::SC_SLOT - 128);
+        const float* sc = reinterpret_cast<const float*>(s_sc + sq * C::SC_SLOT);
+        const float* wsc = reinterpret_cast<const float*>(s_sc + sq * C::SC_SLOT + C::SC_SLOT - 128);
 #pragma unroll
         for (int kk = 0; kk < KS; ++kk) {
           const float as = row_ok ? sc[kk * C::SC_ROW + (tile.y & 3) + j] : 0.f;
@@ -256,7 +278,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
           cB[kk] = as * wsc[4 + x];
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(&empty[s]);
+        if (lane == 0) mbar_arrive(&sempty[sq]);
       }
 #pragma unroll
       for (int kk = 0; kk < KS && !aborted; ++kk, ++g) {
