@@ -51,7 +51,7 @@ class MoeLayout(ctypes.Structure):
     """struct moe_fp8_ds_layout."""
     _fields_ = [(n, ctypes.c_uint64) for n in (
         "total_bytes", "error_word", "topk_ids", "topk_weights", "inv_row", "seg_offsets",
-        "row_token", "block_masks", "block_bases", "inter", "inter_scale", "down", "act", "act_scale", "act16", "inter16")] + [
+        "row_token", "block_masks", "block_bases", "inter", "inter_scale", "down", "act", "act_scale")] + [
         ("row_capacity", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 

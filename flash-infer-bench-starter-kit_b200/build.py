@@ -17,7 +17,7 @@ PKG_DIR = pathlib.Path(__file__).resolve().parent
 CSRC = PKG_DIR / "csrc"
 LIB_NAME = "libmoe_fp8_ds.so"
 LIB_PATH = PKG_DIR / LIB_NAME
-SOURCES = ("api.cu", "route_permute.cu", "gemm_fp8.cu", "gemm_f16.cu", "gemm_tm.cu", "noalloc.cu", "ep.cu")
+SOURCES = ("api.cu", "route_permute.cu", "gemm_fp8.cu", "gemm_tm.cu", "noalloc.cu", "ep.cu")
 HEADERS = ("common.cuh", "kernels.cuh")
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -29,9 +29,9 @@ using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t
                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
-int g_path_override = 0;          // 0 automatic, 1 e4m3 GEMMs, 2 f16-operand GEMMs, 3 tokens-on-M e4m3
+int g_path_override = 0;          // 0 automatic, 1 weights-on-M e4m3 GEMMs, 2 tokens-on-M e4m3 GEMMs
 // From this batch size the layer runs the tokens-on-M e4m3 GEMMs (gemm_tm.cu).
-constexpr int kTmMinTokens = 512;
+constexpr int kTmMinTokens = 1536;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -84,8 +84,6 @@ int pick_bn(int T, int E_l) {
 struct Plan {
   moe_fp8_ds_layout pub;
   int T, E_l, NB, NB8, R_cap, bn1, bn2, grid1, grid2, max_mt1, max_mt2;
-  int bt1, bt2;                     // compiled tile width of each GEMM (>= bn: the tile cap)
-  bool wide;                        // f16-operand GEMMs (gemm_f16.cu), on request only
   bool tm;                          // large batch: tokens-on-M e4m3 GEMMs (gemm_tm.cu)
   uint64_t tiles1, tiles2, sched, counters1, counters2, ready, partials1, partials2, front_sync;
 };
@@ -112,39 +110,23 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
-  P->wide = path_override == 2;
-  P->tm = path_override == 3 || (path_override == 0 && T >= kTmMinTokens);
+  // Tokens-on-M GEMMs (gemm_tm.cu) from kTmMinTokens: their 128-row token
+  // tiles fill the MMA once experts see ~48+ tokens each.  Below that the
+  // weights-on-M GEMMs (gemm_fp8.cu) size the MMA's N to the few tokens an
+  // expert has.  Measured on B200 with 32 local experts, layer us
+  // weights-on-M / tokens-on-M: T=1024 385/424, 2048 575/502, 4096 932/666,
+  // 8192 1697/1093.
+  P->tm = path_override == 2 || (path_override == 0 && T >= kTmMinTokens);
   if (P->tm) {
     // One token tile holds up to 128 rows of one expert (the MMA's M side); a
     // smaller tile cap may be forced for tests.
     auto cap = [](int v) { return v > 0 && v <= 128 ? v : 128; };
     P->bn1 = P->bn2 = cap(bn_override[0]);
-    P->bt1 = P->bt2 = 128;
-  } else if (P->wide) {
-    // f16 kernels accumulate in TMEM, so one tile takes up to 256 tokens.
-    // The widest tiles win, measured on B200 with 32 local experts: each
-    // weight byte a CTA converts then serves the most tokens, and full-height
-    // token boxes (128 / 256 rows, loaded whether or not the tile fills them)
-    // stream faster than boxes cut to the expected rows (GEMM2 at T=4096:
-    // 228 us with 256-row boxes, 283 us with 176).  GEMM1 tiles wider than 128
-    // leave room for one TMEM accumulator only (X1 and X2), so its epilogue no
-    // longer overlaps the next tile; that pays only from ~384 rows per expert
-    // (GEMM1 256 / 128-token tiles, layer us: T=4096 743/618, 8192 941/914,
-    // 12288 1253/1270).
-    const double per_expert = (double)T * kTopK / kExpertsGlobal;
-    const int bn = per_expert >= 384.0 ? 256 : 128;
-    const int bn_2 = 256;
-    P->bn1 = bn_override[0] ? bn_override[0] : bn;
-    P->bn2 = bn_override[1] ? bn_override[1] : bn_2;
-    P->bt1 = P->bn1 > 128 ? 256 : 128;
-    P->bt2 = P->bn2 > 128 ? 256 : 128;
   } else {
     // e4m3 kernels are compiled for 16, 32, 64 and 128 tokens only.
     auto compiled = [](int v) { return v == 16 || v == 32 || v == 64 || v == 128; };
     P->bn1 = compiled(bn_override[0]) ? bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
     P->bn2 = compiled(bn_override[1]) ? bn_override[1] : bn_auto;
-    P->bt1 = P->bn1;
-    P->bt2 = P->bn2;
   }
 
   auto max_mt = [&](int bn) {
@@ -172,24 +154,17 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   P->counters2 = take((uint64_t)P->max_mt2 * (kHidden / 128) * 4);
   P->ready = take((uint64_t)E_l * 4);
   P->pub.row_token = take(R * 4);
-  const uint64_t R8 = P->wide ? 0 : R, R16 = P->wide ? R : 0;   // only the active path's buffers
-  // (the tokens-on-M GEMMs use the e4m3 buffers; their intermediate holds the
-  // hi and lo planes [2][R_cap][2048] in the same bytes as the row pairs)
-  P->pub.act = take(R8 * kHidden);
-  P->pub.act_scale = take(R8 * kHiddenBlocks * 4);
-  P->pub.inter = take(2 * R8 * kInter);
-  P->pub.inter_scale = take(R8 * kInterBlocks * 4);
-  P->pub.act16 = take(R16 * kHidden * 2);
-  P->pub.inter16 = take(R16 * kInter * 2);
+  // (the tokens-on-M GEMMs' intermediate holds the hi and lo planes
+  // [2][R_cap][2048] in the same bytes as the weights-on-M row pairs)
+  P->pub.act = take(R * kHidden);
+  P->pub.act_scale = take(R * kHiddenBlocks * 4);
+  P->pub.inter = take(2 * R * kInter);
+  P->pub.inter_scale = take(R * kInterBlocks * 4);
   P->pub.down = take(R * kHidden * 4);
   if (P->tm) {
     P->grid1 = P->grid2 = sm_count;
     P->partials1 = take(gemm_tm_partials_bytes(P->grid1));
     P->partials2 = take(gemm_tm_partials_bytes(P->grid2));
-  } else if (P->wide) {
-    P->grid1 = P->grid2 = sm_count;
-    P->partials1 = take(gemm_f16_partials_bytes(1, P->bt1, P->grid1));
-    P->partials2 = take(gemm_f16_partials_bytes(2, P->bt2, P->grid2));
   } else {
     P->grid1 = sm_count * gemm_ctas_per_sm(1, P->bn1);   // persistent: every resident CTA slot
     P->grid2 = sm_count * gemm_ctas_per_sm(2, P->bn2);
@@ -213,30 +188,6 @@ bool encode_kmajor(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, 
                         box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
-}
-
-// e4m3 weights [rows, K] as {x = byte inside a 64-byte K atom, atom, row};
-// box = 64 bytes x 1 atom x 128 rows, unswizzled (converter staging).
-bool encode_w8_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows = 128) {
-  cuuint64_t dims[3] = {64, K / 64, rows};
-  cuuint64_t strides[2] = {64, K};
-  cuuint32_t box[3] = {64, 1, box_rows};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
-// f16 tokens [rows, K] as {x = element inside a 64-element K atom, atom, row};
-// box = 64 elements x 1 atom x box_rows rows with 128-byte swizzle.
-bool encode_b16_atoms(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows) {
-  cuuint64_t dims[3] = {64, K / 64, rows};
-  cuuint64_t strides[2] = {128, K * 2};
-  cuuint32_t box[3] = {64, 1, box_rows};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides, box,
-                  estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 // K-major e4m3 operand in two planes, viewed as {128 B of a K block, row, K
@@ -338,17 +289,9 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   float* down = reinterpret_cast<float*>(at(P.pub.down));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
 
-  __half* act16 = reinterpret_cast<__half*>(at(P.pub.act16));
-  __half* inter16 = reinterpret_cast<__half*>(at(P.pub.inter16));
   CUtensorMap tm_w1, tm_b1, tm_w2, tm_b2;
   CUtensorMap tm_bs1, tm_ws1, tm_bs2, tm_ws2;   // tokens-on-M GEMMs: block scales
-  if (P.wide) {
-    if (!encode_w8_atoms(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out) ||
-        !encode_b16_atoms(&tm_b1, act16, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1) ||
-        !encode_w8_atoms(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden) ||
-        !encode_b16_atoms(&tm_b2, inter16, kInter, (uint64_t)P.R_cap, (uint32_t)P.bn2))
-      return MOE_ERR_INVALID_ARGUMENT;
-  } else if (P.tm) {
+  if (P.tm) {
     // tokens-on-M GEMMs: 128-row boxes of tokens (GEMM2: hi plane rows r, lo
     // plane rows R_cap + r) and of weights
     const uint32_t ks1 = (uint32_t)gemm_tm_k_per_stage(1), ks2 = (uint32_t)gemm_tm_k_per_stage(2);
@@ -377,7 +320,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   }
 
   cudaError_t ce;
-  const bool front = !routed && T <= kFrontMaxTokens && !P.wide && !P.tm;
+  const bool front = !routed && T <= kFrontMaxTokens && !P.tm;
   if (front) {
     // Small batch: routing, row assignment and gather in one launch.
     mark_stage(0, s);
@@ -402,7 +345,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
                         a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale,
-                        P.wide ? act16 : nullptr, s);
+                        s);
     if (ce != cudaSuccess) return cuda_fail(ce);
   }
 
@@ -413,12 +356,9 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.early_start = front ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
-  g1.inter16 = inter16;
-  g1.box_rows = P.bn1;
   g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
   g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
   ce = P.tm     ? launch_gemm_tm(1, &tm_w1, &tm_b1, &tm_bs1, &tm_ws1, g1, P.grid1, s)
-       : P.wide ? launch_gemm_f16(1, P.bt1, &tm_w1, &tm_b1, g1, P.grid1, s)
                 : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);
   if (ce != cudaSuccess) return cuda_fail(ce);
 
@@ -429,10 +369,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g2.early_start = front ? 1 : 0; g2.partials = reinterpret_cast<float*>(at(P.partials2));
   g2.inter = nullptr; g2.inter_scale = nullptr; g2.down = down; g2.err = err; g2.R_cap = P.R_cap;
   mark_stage(4, s);
-  g2.inter16 = nullptr;
-  g2.box_rows = P.bn2;
   ce = P.tm     ? launch_gemm_tm(2, &tm_w2, &tm_b2, &tm_bs2, &tm_ws2, g2, P.grid2, s)
-       : P.wide ? launch_gemm_f16(2, P.bt2, &tm_w2, &tm_b2, g2, P.grid2, s)
                 : launch_gemm(2, P.bn2, &tm_w2, &tm_b2, g2, P.grid2, s);
   if (ce != cudaSuccess) return cuda_fail(ce);
 
@@ -591,7 +528,7 @@ int moe_fp8_ds_set_stage_events(void* const* events, int32_t count) {
 }
 
 int moe_fp8_ds_set_path_override(int32_t mode) {
-  if (mode < 0 || mode > 3) return MOE_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 2) return MOE_ERR_INVALID_ARGUMENT;
   std::lock_guard<std::mutex> lk(g_mu);
   g_path_override = mode;
   return MOE_OK;

@@ -358,26 +358,6 @@ __device__ __forceinline__ uint32_t elect_one_lane() {
   return pred;
 }
 
-// 16 e4m3 values (one uint4) times `scale` -> 16 f16 (two uint4), each
-// value decoded exactly, scaled in fp32 and rounded to nearest f16.
-__device__ __forceinline__ void e4m3x16_to_f16(uint4 src, float scale, uint4& lo, uint4& hi) {
-  const uint32_t w[4] = {src.x, src.y, src.z, src.w};
-  uint32_t out[8];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __nv_fp8x2_storage_t pair = static_cast<__nv_fp8x2_storage_t>((w[i] >> (16 * h)) & 0xFFFF);
-      const __half2 hf = __half2(__nv_cvt_fp8x2_to_halfraw2(pair, __NV_E4M3));
-      const float2 f = __half22float2(hf);
-      const __half2 b = __floats2half2_rn(f.x * scale, f.y * scale);
-      out[i * 2 + h] = *reinterpret_cast<const uint32_t*>(&b);
-    }
-  }
-  lo = make_uint4(out[0], out[1], out[2], out[3]);
-  hi = make_uint4(out[4], out[5], out[6], out[7]);
-}
-
 // fp32 -> e4m3 with round-to-nearest-even and saturation to +-448.
 __device__ __forceinline__ uint8_t f32_to_e4m3(float x) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3));

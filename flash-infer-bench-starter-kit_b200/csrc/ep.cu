@@ -142,7 +142,9 @@ __global__ void __launch_bounds__(256) ep_unpack_kernel(const uint8_t* __restric
 
 // out[t] = bf16( sum over r ascending, slot[t][r] >= 0, of float(part[slot[t][r]]) ),
 // the sum starting from +0.  Grid (T, 7); 128 threads x 8 columns.
-__global__ void __launch_bounds__(128) ep_combine_kernel(const __nv_bfloat16* __restrict__ part,
+// Partials arrive in fp32 (each rank's sum over its own picks, not rounded),
+// so the only rounding to bf16 is the final one, as on one GPU.
+__global__ void __launch_bounds__(128) ep_combine_kernel(const float* __restrict__ part,
                                                           const int32_t* __restrict__ slot, int world,
                                                           __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
@@ -153,14 +155,10 @@ __global__ void __launch_bounds__(128) ep_combine_kernel(const __nv_bfloat16* __
   for (int r = 0; r < world; ++r) {
     const int s = __ldg(slot + (size_t)t * world + r);
     if (s < 0) continue;
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(part + (size_t)s * kHidden + col));
-    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-    for (int x = 0; x < 4; ++x) {
-      const float2 f = __bfloat1622float2(h[x]);
-      acc[2 * x] += f.x;
-      acc[2 * x + 1] += f.y;
-    }
+    const float4* src = reinterpret_cast<const float4*>(part + (size_t)s * kHidden + col);
+    const float4 a = __ldg(src), b = __ldg(src + 1);
+    acc[0] += a.x; acc[1] += a.y; acc[2] += a.z; acc[3] += a.w;
+    acc[4] += b.x; acc[5] += b.y; acc[6] += b.z; acc[7] += b.w;
   }
   uint4 o;
   __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
@@ -226,7 +224,7 @@ MOE_API int moe_fp8_ds_ep_combine(const void* partials, const int32_t* slot, int
   if (!slot || !output) return MOE_ERR_INVALID_ARGUMENT;
   if (!aligned16(output) || (partials && !aligned16(partials))) return MOE_ERR_MISALIGNED;
   ep_combine_kernel<<<dim3(num_tokens, kHidden / (128 * 8)), 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const __nv_bfloat16*>(partials), slot, world, static_cast<__nv_bfloat16*>(output));
+      static_cast<const float*>(partials), slot, world, static_cast<__nv_bfloat16*>(output));
   return launch_status();
 }
 

@@ -15,7 +15,6 @@ struct GemmParams {
   int* ready;                 // per local expert: GEMM1 units finished (GEMM1 adds, GEMM2 waits)
   const int32_t* seg;         // per-expert row offsets (GEMM2: rows of expert e)
   int bn_prev;                // GEMM2: GEMM1's token-tile width
-  int box_rows;               // f16 GEMMs: rows of the token operand's TMA box (the tile cap)
   // e4m3 GEMM1 after the fused front kernel: front_sync[0] = 1 once the tile
   // lists are written, front_sync[1] counts front CTAs whose gather is done.
   // GEMM1 starts streaming weights at the first and reads activations after
@@ -27,7 +26,6 @@ struct GemmParams {
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048] (row pairs, or hi/lo planes)
   float* inter_scale;         // GEMM1 output: [16, R_cap]
   float* down;                // GEMM2 output: fp32 [R_cap, 7168]
-  __half* inter16;            // f16 GEMM1 output (large batches): [R_cap, 2048]
   int* err;
   int R_cap;
 };
@@ -106,10 +104,6 @@ int gemm_tm_scale_box_cols();
 cudaError_t launch_gemm_tm(int kind, const CUtensorMap* tm_w, const CUtensorMap* tm_b, const CUtensorMap* tm_bs,
                            const CUtensorMap* tm_ws, const GemmParams& p, int grid, cudaStream_t st);
 
-// f16-operand GEMMs (gemm_f16.cu).
-size_t gemm_f16_partials_bytes(int kind, int bn, int grid);
-cudaError_t launch_gemm_f16(int kind, int bn, const CUtensorMap* tm_w, const CUtensorMap* tm_b,
-                             const GemmParams& p, int grid, cudaStream_t st);
 
 cudaError_t launch_route(bool from_ids, const float* logits, const void* bias, int T,
                          float scaling, int local_offset, int E_l, int32_t* ids, float* w,
@@ -121,7 +115,7 @@ cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB,
 cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
-                           uint8_t* act, float* act_scale, __half* act16, cudaStream_t st);
+                           uint8_t* act, float* act_scale, cudaStream_t st);
 // Routing + row assignment + activation gather in one launch, T <= kFrontMaxTokens.
 cudaError_t launch_front(const float* logits, const void* bias, int T, float scaling, int local_offset,
                          int E_l, int R_cap, int bn1, int bn2, int nt1, int nt2, const void* hidden,

@@ -348,8 +348,7 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
                const int32_t* __restrict__ bases, int T, int E_l, int local_offset, int R_cap,
                const uint8_t* __restrict__ hidden, const float* __restrict__ hs_scale,
                int32_t* __restrict__ inv_row, int32_t* __restrict__ row_token,
-               uint8_t* __restrict__ act, float* __restrict__ act_scale,
-               __half* __restrict__ act16) {
+               uint8_t* __restrict__ act, float* __restrict__ act_scale) {
   __shared__ int s_row[kPermBlock * kTopK];
   griddep_wait();
   griddep_launch_dependents();
@@ -383,9 +382,7 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
   }
   __syncthreads();
   // copy: 16-byte vectors of the compacted pairs, kBatch loads in flight per
-  // thread before the stores.  With act16 the rows are written in f16 with
-  // their 1x128 scales applied (operand of the f16 GEMMs); otherwise as e4m3
-  // plus the scales.
+  // thread before the stores
   constexpr int kVec = kGatherChunk / 16;
   constexpr int kBatch = 4;
   const size_t col = (size_t)blockIdx.y * kGatherChunk;
@@ -405,28 +402,15 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
       const int v = v0 + u * blockDim.x;
       if (v >= nvec) break;
       const int2 rt = s_list[v / kVec];
-      const int off = (v % kVec) * 16;
-      if (act16) {
-        const int kb = (int)((col + off) / kBlock);
-        const float sc = __ldg(hs_scale + (size_t)kb * T + rt.y);
-        uint4 lo, hi;
-        e4m3x16_to_f16(val[u], sc, lo, hi);
-        uint4* dst = reinterpret_cast<uint4*>(act16 + (size_t)rt.x * kHidden + col + off);
-        dst[0] = lo;
-        dst[1] = hi;
-      } else {
-        *reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden + col + off) = val[u];
-      }
+      *reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden + col + (v % kVec) * 16) = val[u];
     }
   }
-  if (!act16) {
-    const int r = s_row[threadIdx.x];
-    if (r >= 0) {
-      const int kb0 = blockIdx.y * (kGatherChunk / kBlock);
+  const int r = s_row[threadIdx.x];
+  if (r >= 0) {
+    const int kb0 = blockIdx.y * (kGatherChunk / kBlock);
 #pragma unroll
-      for (int q = 0; q < kGatherChunk / kBlock; ++q)
-        act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + t);
-    }
+    for (int q = 0; q < kGatherChunk / kBlock; ++q)
+      act_scale[(size_t)(kb0 + q) * R_cap + r] = __ldg(hs_scale + (size_t)(kb0 + q) * T + t);
   }
 }
 
@@ -738,12 +722,12 @@ cudaError_t launch_scan(const uint8_t* masks8, int NB8p, int32_t* bases, int NB,
 cudaError_t launch_scatter(const int32_t* ids, const uint8_t* masks8, int NB8p, const int32_t* bases, int T,
                            int E_l, int local_offset, int R_cap, const void* hidden,
                            const float* hs_scale, int32_t* inv_row, int32_t* row_token,
-                           uint8_t* act, float* act_scale, __half* act16, cudaStream_t st) {
+                           uint8_t* act, float* act_scale, cudaStream_t st) {
   const int nb = (T + kPermBlock - 1) / kPermBlock;
   if (nb == 0) return cudaSuccess;
   return launch_pdl(scatter_kernel, dim3(nb, kGatherChunks), dim3(kPermBlock * kTopK), 0, st, ids,
                     masks8, NB8p, bases, T, E_l, local_offset, R_cap, static_cast<const uint8_t*>(hidden),
-                    hs_scale, inv_row, row_token, act, act_scale, act16);
+                    hs_scale, inv_row, row_token, act, act_scale);
 }
 
 cudaError_t launch_front(const float* logits, const void* bias, int T, float scaling, int local_offset,

@@ -13,8 +13,9 @@ batch of tokens:
    moves only real rows;
 3. each rank runs the layer's expert part (``moe_fp8_ds_run_routed``) on the
    rows it received, for its own experts only;
-4. combine: partial results go back to the token's home rank, which sums
-   them in ascending rank order in fp32 and writes bf16.
+4. combine: partial results go back to the token's home rank in fp32 (each
+   rank's unrounded sum over its own experts), which sums them in ascending
+   rank order in fp32 and rounds to bf16 once, as the single-GPU layer does.
 
 Rows are ordered by (destination rank, token) and the combine sums in a fixed
 rank order, so the result is deterministic.  The exchange uses
@@ -159,8 +160,8 @@ class LibPlumbing:
         return hidden, scale, ids, w
 
     def combine(self, back, slot, T, output):
-        if back.dtype != torch.bfloat16 or output.dtype != torch.bfloat16 or not output.is_contiguous():
-            raise TypeError("the library combine takes bf16 partials and a contiguous bf16 output")
+        if back.dtype != torch.float32 or output.dtype != torch.bfloat16 or not output.is_contiguous():
+            raise TypeError("the library combine takes fp32 partials and a contiguous bf16 output")
         slot = slot.to(torch.int32).contiguous()
         self._L.check(self._lib.moe_fp8_ds_ep_combine(self._p(back), self._p(slot), T, slot.shape[1],
                                                       self._p(output), self._s(output.device)),
@@ -187,6 +188,8 @@ class ExpertParallelMoE:
             raise ValueError(f"{E_GLOBAL} experts do not split over {self.world} ranks")
         self.E_l = E_GLOBAL // self.world
         self.last_stats = {}
+        self.profile = False
+        self._events = None
 
     @torch.no_grad()
     def forward(self, routing_logits, routing_bias, hidden_states, hidden_states_scale,
@@ -196,23 +199,55 @@ class ExpertParallelMoE:
             raise ValueError(f"rank holds {gemm1_weights.shape[0]} experts, expected {self.E_l}")
         T = hidden_states.shape[0]
         pl = self.plumbing
+        mark = self._marker(hidden_states.device)
+        mark("start")
         ids, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
+        mark("route")
         counts, slot, src_token = pl.plan(ids, self.world, self.E_l)
-        # count exchange, then the row all-to-all moves only real rows
+        mark("plan")
+        # count exchange, then the row all-to-all moves only real rows (the
+        # split sizes must be on the host: one device-to-host read per step)
         recv_counts = torch.empty_like(counts)
         dist.all_to_all_single(recv_counts, counts, group=self.group)
         in_splits, out_splits = counts.tolist(), recv_counts.tolist()
+        mark("count_a2a")
         send = pl.pack(ids, w, hidden_states, hidden_states_scale, src_token, sum(in_splits))
+        mark("pack")
         recv = torch.empty(sum(out_splits), ROW_BYTES, dtype=torch.uint8, device=send.device)
         dist.all_to_all_single(recv, send, out_splits, in_splits, group=self.group)
+        mark("row_a2a")
         r_hidden, r_scale, r_ids, r_w = pl.unpack(recv)
         part = self.expert_fn(r_ids, r_w, r_hidden, r_scale, gemm1_weights, gemm1_weights_scale,
                               gemm2_weights, gemm2_weights_scale, self.rank * self.E_l)
+        mark("experts")
         back = torch.empty(send.shape[0], H, dtype=part.dtype, device=part.device)
         dist.all_to_all_single(back, part, in_splits, out_splits, group=self.group)
+        mark("partial_a2a")
         pl.combine(back, slot, T, output)
+        mark("combine")
         self.last_stats = {"sent_rows": int(send.shape[0]), "recv_rows": int(recv.shape[0])}
         return output
+
+    def _marker(self, device):
+        """Per-phase CUDA events when ``self.profile`` is set (read with ``phase_ms``)."""
+        if not self.profile or device.type != "cuda":
+            self._events = None
+            return lambda name: None
+        self._events = []
+
+        def mark(name):
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self._events.append((name, ev))
+        return mark
+
+    def phase_ms(self):
+        """{phase: ms} of the last profiled call (synchronises the device)."""
+        if not self._events:
+            return {}
+        torch.cuda.synchronize()
+        ev = self._events
+        return {ev[i][0]: ev[i - 1][1].elapsed_time(ev[i][1]) for i in range(1, len(ev))}
 
     __call__ = forward
 
@@ -237,9 +272,9 @@ def from_library(group=None):
 
     def expert_fn(ids, w, hidden, scale, w13, s13, w2, s2, offset):
         R = hidden.shape[0]
-        out = torch.empty(R, H, dtype=torch.bfloat16, device=hidden.device)
-        args = K.build_args(None, None, hidden, scale, w13, s13, w2, s2, offset, 1.0, out,
-                            topk_ids=ids, topk_weights=w)
+        out = torch.empty(R, H, dtype=torch.float32, device=hidden.device)
+        args = K.build_args(None, None, hidden, scale, w13, s13, w2, s2, offset, 1.0, None,
+                            topk_ids=ids, topk_weights=w, output_f32=out)
         if R:
             ws = K.get_workspace(hidden.device, K.workspace_bytes(R, w13.shape[0]))
             K.run_with_workspace(args, ws, routed=True)

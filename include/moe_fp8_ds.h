@@ -92,15 +92,15 @@ typedef struct moe_fp8_ds_layout {
   uint64_t row_token;       /* int32 [R_cap]  source token of each permuted row   */
   uint64_t block_masks;     /* uint8 [E_l, 4*ceil(T/32)] bit w: token 8g+w picked e */
   uint64_t block_bases;     /* int32 [ceil(T/32), E_l] first row of block b in expert e */
-  uint64_t inter;           /* e4m3  [2*R_cap, 2048] SwiGLU output, rows (2r, 2r+1) = (hi, lo) */
-  uint64_t inter_scale;     /* fp32  [16, R_cap]  scale of hi; lo uses scale/16    */
+  uint64_t inter;           /* e4m3  SwiGLU output in two terms: weights-on-M GEMMs
+                               [R_cap][2][2048] rows (hi, lo), lo on scale/16;
+                               tokens-on-M GEMMs [2][R_cap][2048] planes (hi, lo)
+                               on one scale                                      */
+  uint64_t inter_scale;     /* fp32  [16, R_cap]  1x128 scales of the SwiGLU output */
   uint64_t down;            /* fp32  [R_cap, 7168] GEMM2 output per permuted row  */
   uint64_t act;             /* e4m3  [R_cap, 7168] permuted hidden rows (e4m3 GEMM1 input) */
   uint64_t act_scale;       /* fp32  [56, R_cap]  their 1x128 scales              */
-  /* The f16-operand GEMMs (T >= 1536) use these instead of act/act_scale/inter: */
-  uint64_t act16;           /* f16   [R_cap, 7168] permuted rows, scales applied  */
-  uint64_t inter16;         /* f16   [R_cap, 2048] SwiGLU output                  */
-  int32_t row_capacity;     /* R_cap = T * min(8, E_l)                            */
+  int32_t row_capacity;     /* R_cap = T * min(8, E_l) rounded up to 16           */
   int32_t reserved;
 } moe_fp8_ds_layout;
 
@@ -175,18 +175,16 @@ MOE_API const char* moe_fp8_ds_status_string(int status);
 
 /* Tuning knob: force the token-tile cap (a multiple of 16, at most 256) of
  * GEMM1 and GEMM2 for calls on this process; 0 restores the automatic choice
- * from T.  The weights-on-M e4m3 GEMMs take 16, 32, 64 or 128 and use the
- * automatic choice for other values; the f16 GEMMs take any; the tokens-on-M
- * GEMMs take the GEMM1 value (at most 128) for both.  Takes effect for the
- * next call (workspace size included). */
+ * from T.  The weights-on-M GEMMs take 16, 32, 64 or 128 and use the
+ * automatic choice for other values; the tokens-on-M GEMMs take the GEMM1
+ * value (at most 128) for both.  Takes effect for the next call (workspace
+ * size included). */
 MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Tuning knob: 0 = automatic GEMM family (e4m3 GEMMs with weights on the
- * MMA's M side for T < 512, e4m3 GEMMs with tokens on M from 512 tokens),
- * 1 = always weights-on-M e4m3, 2 = always f16-operand GEMMs (block scales
- * folded into f16 operands; never chosen automatically), 3 = always
- * tokens-on-M e4m3.  Takes effect for the next call (workspace size
- * included). */
+ * MMA's M side for T < 1536, e4m3 GEMMs with tokens on M from 1536 tokens),
+ * 1 = always weights-on-M, 2 = always tokens-on-M.  Takes effect for the next
+ * call (workspace size included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);
 
 /* Profiling hook: when `count` is 7, later calls on this process record
@@ -232,8 +230,9 @@ MOE_API int moe_fp8_ds_ep_unpack(const void* recv, int32_t rows, void* hidden_st
                                  int32_t* topk_ids, float* topk_weights, void* stream);
 
 /* output[t] = bf16(sum over ranks r ascending with slot[t][r] >= 0 of
- * partials[slot[t][r]]), the sum in fp32 from +0; partials bf16 [S, 7168]
- * in send-row order, output bf16 [T, 7168].                                 */
+ * partials[slot[t][r]]), the sum in fp32 from +0; partials fp32 [S, 7168]
+ * in send-row order (each rank's unrounded sum over its own experts), output
+ * bf16 [T, 7168].                                                           */
 MOE_API int moe_fp8_ds_ep_combine(const void* partials, const int32_t* slot, int32_t num_tokens, int32_t world,
                                   void* output, void* stream);
 

@@ -81,7 +81,7 @@ def _worker(rank, world, port, T, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_ep_protocol_matches_single_process(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

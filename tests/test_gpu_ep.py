@@ -1,7 +1,8 @@
-"""GPU, 2 processes over NCCL: the expert-parallel layer equals the
-single-GPU layer that holds all 256 experts (within the layer tolerance; the
-EP path adds one bf16 rounding of each rank's partial sum).  Skipped on a box
-with fewer than two GPUs."""
+"""GPU, 2 processes over NCCL: the expert-parallel layer against the CPU
+oracle (the first tokens of each rank, through every expert they pick) and
+against the single-GPU layer that holds all 256 experts, both within the
+layer tolerance; partials travel in fp32, so the only bf16 rounding is the
+final one.  Skipped on a box with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -52,6 +53,18 @@ def _worker(rank, world, port, T, q):
         torch.cuda.synchronize()
         r, o = ref.float(), out.float()
         bad = int(((o - r).abs() > ATOL + RTOL * r.abs()).sum())
+        # oracle for the first 4 tokens: their experts only, dequantised on the host
+        from oracle import moe_ref
+        n = 4
+        lc, bc = logits[:n].cpu(), bias.cpu()
+        ids, wts, _ = moe_ref.route(lc, bc, 2.5)
+        used = sorted(set(ids.flatten().tolist()))
+        acc = torch.zeros(n, 7168)
+        for e in used:
+            acc += moe_ref.experts_forward(ids, wts, hs[:n].cpu(), hss[:, :n].contiguous().cpu(),
+                                           w13[e:e + 1].cpu(), s13[e:e + 1].cpu(), w2[e:e + 1].cpu(),
+                                           s2[e:e + 1].cpu(), e)
+        bad += int(((o[:n].cpu() - acc).abs() > ATOL + RTOL * acc.abs()).sum())
         q.put((rank, bad, bool(torch.isnan(o).any()), float((o - r).abs().max()),
                torch.equal(out.view(torch.int16), out2.view(torch.int16)), layer.last_stats))
     except Exception:

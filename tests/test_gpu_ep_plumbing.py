@@ -53,7 +53,7 @@ def test_plumbing_matches_torch(pkg, cuda_dev, world, T, hot):
         assert torch.equal(a.view(torch.uint8).cpu() if a.dtype == torch.float8_e4m3fn else a.cpu(),
                            b.view(torch.uint8).cpu() if b.dtype == torch.float8_e4m3fn else b.cpu())
 
-    back = (torch.randn(S, 7168, device=cuda_dev) * 4).to(torch.bfloat16)
+    back = torch.randn(S, 7168, device=cuda_dev) * 4
     out1 = torch.full((T, 7168), float("nan"), dtype=torch.bfloat16, device=cuda_dev)
     out0 = torch.empty(T, 7168, dtype=torch.bfloat16, device=cuda_dev)
     lib.combine(back, s1, T, out1)

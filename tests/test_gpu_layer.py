@@ -24,7 +24,7 @@ from conftest import cached_inputs, load_golden
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 1e-2, 2e-2
-TM_MIN_TOKENS = 512          # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
+TM_MIN_TOKENS = 1536         # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
 
 
 def _mods():
@@ -37,7 +37,7 @@ def to_dev(inp, dev):
 
 def run_layer(pkg, inp_dev, ws=None, bn=(0, 0), path=0):
     """Run through the C ABI with an explicit workspace; returns (output, ws, layout).
-    ``bn`` forces the token-tile widths, ``path`` the GEMM family (1 e4m3, 2 f16)."""
+    ``bn`` forces the token-tile widths, ``path`` the GEMM family (1 weights-on-M, 2 tokens-on-M)."""
     K, L = _mods()
     lib = L.load()
     L.check(lib.moe_fp8_ds_set_tile_override(int(bn[0]), int(bn[1])), "set_tile_override")
@@ -151,7 +151,7 @@ def test_layer_matches_reference_golden(name, pkg, oracle, cuda_dev):
 
 # ---------------------------------------------------------------------------- stages
 STAGE_CASES = [
-    # T, E_l, offset, seed, skew, (bn1, bn2[, GEMM family])
+    # T, E_l, offset, seed, skew, (bn1, bn2[, GEMM family: 1 weights-on-M, 2 tokens-on-M])
     (1, 8, 0, 11, 0.0, (0, 0)),
     (16, 8, 0, 12, 0.0, (0, 0)),
     (64, 32, 0, 13, 0.0, (0, 0)),
@@ -160,17 +160,14 @@ STAGE_CASES = [
     (200, 8, 0, 14, 3.0, (16, 32)),        # 32-token GEMM2 tiles (four K blocks per stage)
     (200, 8, 0, 14, 3.0, (128, 128)),
     (130, 16, 16, 15, 0.0, (64, 32)),
-    (300, 8, 0, 16, 0.0, (0, 0)),          # T > 256: 3-kernel front end, weights-on-M e4m3 GEMMs
-    (300, 8, 0, 16, 0.0, (0, 0, 2)),       # f16-operand GEMMs forced at a small batch (64-token tiles)
-    (300, 8, 0, 16, 0.0, (0, 0, 3)),       # tokens-on-M GEMMs forced at a small batch (ragged tiles)
-    (64, 32, 0, 13, 0.0, (0, 0, 3)),       # tokens-on-M GEMMs, a few rows per expert, many stream-K splits
-    (4200, 8, 0, 17, 0.0, (0, 0, 1)),      # weights-on-M e4m3 GEMMs forced, 64/128-token tiles, many rows
-    (4200, 8, 0, 17, 0.0, (0, 0)),         # tokens-on-M GEMMs by default from 512 tokens
-    (4200, 8, 0, 17, 0.0, (48, 0, 3)),     # tokens-on-M GEMMs with 48-row tiles
-    (4200, 8, 0, 17, 0.0, (96, 176, 2)),   # f16 GEMMs, tile caps below the compiled widths
-    (4200, 8, 0, 17, 0.0, (208, 0, 2)),    # f16 GEMM1 with 256-token tiles (one TMEM accumulator)
-    (2100, 8, 0, 18, 3.0, (0, 0, 2)),      # f16 GEMMs, skewed routing: hot experts with many tiles
-    (2100, 8, 0, 18, 3.0, (0, 0)),         # tokens-on-M GEMMs, skewed routing
+    (300, 8, 0, 16, 0.0, (0, 0)),          # T > 256: 3-kernel front end, weights-on-M GEMMs
+    (300, 8, 0, 16, 0.0, (0, 0, 2)),       # tokens-on-M GEMMs forced at a small batch (ragged tiles)
+    (64, 32, 0, 13, 0.0, (0, 0, 2)),       # tokens-on-M GEMMs, a few rows per expert, many stream-K splits
+    (4200, 8, 0, 17, 0.0, (0, 0, 1)),      # weights-on-M GEMMs forced, 64/128-token tiles, many rows
+    (4200, 8, 0, 17, 0.0, (0, 0)),         # tokens-on-M GEMMs by default from 1536 tokens
+    (4200, 8, 0, 17, 0.0, (48, 0, 2)),     # tokens-on-M GEMMs with 48-row tiles
+    (2100, 8, 0, 18, 3.0, (0, 0)),         # tokens-on-M GEMMs, skewed routing: hot experts with many tiles
+    (2100, 8, 0, 18, 3.0, (0, 0, 1)),      # weights-on-M GEMMs, skewed routing
 ]
 
 
@@ -210,8 +207,7 @@ def check_stages(pkg, oracle, inp, inp_dev, bn, path, experts=None):
     E_l = inp["gemm1_weights"].shape[0]
     off = inp["local_expert_offset"]
     out, ws, lay = run_layer(pkg, inp_dev, bn=bn, path=path)
-    wide = path == 2
-    tm = path == 3 or (path == 0 and T >= TM_MIN_TOKENS)
+    tm = path == 2 or (path == 0 and T >= TM_MIN_TOKENS)
     R = lay.row_capacity
     # routing
     ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"],
@@ -231,32 +227,26 @@ def check_stages(pkg, oracle, inp, inp_dev, bn, path, experts=None):
     assert torch.equal(row_tok, row_tok_ref)
     A = oracle.dequant_hidden(inp["hidden_states"], inp["hidden_states_scale"])
     down = ws_view(ws, lay.down, R * 7168, torch.float32).view(R, 7168)[:nrows].cpu()
-    if not wide:
-        # e4m3 GEMMs: permuted e4m3 rows + scales, two-term e4m3 intermediate
-        act = ws_view(ws, lay.act, R * 7168, torch.uint8).view(R, 7168)[:nrows].cpu()
-        assert torch.equal(act, inp["hidden_states"].view(torch.uint8)[row_tok])
-        act_sc = ws_view(ws, lay.act_scale, 56 * R, torch.float32).view(56, R)[:, :nrows].cpu()
-        assert torch.equal(act_sc, inp["hidden_states_scale"][:, row_tok])
-        isc = ws_view(ws, lay.inter_scale, 16 * R, torch.float32).view(16, R)[:, :nrows].cpu().t()
-        if tm:
-            # tokens-on-M GEMMs: hi and lo planes on the same 1x128 scale
-            inter = ws_view(ws, lay.inter, 2 * R * 2048, torch.uint8).view(2, R, 2048)[:, :nrows].cpu()
-            hi = oracle.fp8_to_f32(inter[0]).view(nrows, 16, 128)
-            lo = oracle.fp8_to_f32(inter[1]).view(nrows, 16, 128)
-            deq = ((hi + lo) * isc.unsqueeze(-1)).view(nrows, 2048)
-        else:
-            # weights-on-M GEMMs: row pairs (hi, lo), lo on a 16x finer scale
-            inter = ws_view(ws, lay.inter, 2 * R * 2048, torch.uint8).view(R, 2, 2048)[:nrows].cpu()
-            hi = oracle.fp8_to_f32(inter[:, 0]).view(nrows, 16, 128)
-            lo = oracle.fp8_to_f32(inter[:, 1]).view(nrows, 16, 128)
-            deq = (hi * isc.unsqueeze(-1) + lo * (isc / 16).unsqueeze(-1)).view(nrows, 2048)
-        g1_tol, g2_tol = 3e-3, 1e-4
+    # permuted e4m3 rows + scales
+    act = ws_view(ws, lay.act, R * 7168, torch.uint8).view(R, 7168)[:nrows].cpu()
+    assert torch.equal(act, inp["hidden_states"].view(torch.uint8)[row_tok])
+    act_sc = ws_view(ws, lay.act_scale, 56 * R, torch.float32).view(56, R)[:, :nrows].cpu()
+    assert torch.equal(act_sc, inp["hidden_states_scale"][:, row_tok])
+    # two-term e4m3 intermediate
+    isc = ws_view(ws, lay.inter_scale, 16 * R, torch.float32).view(16, R)[:, :nrows].cpu().t()
+    if tm:
+        # tokens-on-M GEMMs: hi and lo planes on the same 1x128 scale
+        inter = ws_view(ws, lay.inter, 2 * R * 2048, torch.uint8).view(2, R, 2048)[:, :nrows].cpu()
+        hi = oracle.fp8_to_f32(inter[0]).view(nrows, 16, 128)
+        lo = oracle.fp8_to_f32(inter[1]).view(nrows, 16, 128)
+        deq = ((hi + lo) * isc.unsqueeze(-1)).view(nrows, 2048)
     else:
-        # f16-operand GEMMs: rows in f16 with scales applied, f16 intermediate
-        act16 = ws_view(ws, lay.act16, R * 7168, torch.float16).view(R, 7168)[:nrows].cpu()
-        assert torch.equal(act16, A[row_tok].to(torch.float16))
-        deq = ws_view(ws, lay.inter16, R * 2048, torch.float16).view(R, 2048)[:nrows].cpu().float()
-        g1_tol, g2_tol = 3e-3, 2e-3            # f16 operands: 2^-12 relative per element
+        # weights-on-M GEMMs: row pairs (hi, lo), lo on a 16x finer scale
+        inter = ws_view(ws, lay.inter, 2 * R * 2048, torch.uint8).view(R, 2, 2048)[:nrows].cpu()
+        hi = oracle.fp8_to_f32(inter[:, 0]).view(nrows, 16, 128)
+        lo = oracle.fp8_to_f32(inter[:, 1]).view(nrows, 16, 128)
+        deq = (hi * isc.unsqueeze(-1) + lo * (isc / 16).unsqueeze(-1)).view(nrows, 2048)
+    g1_tol, g2_tol = 3e-3, 1e-4
     for e in (range(E_l) if experts is None else experts):
         r0, r1 = int(seg[e]), int(seg[e + 1])
         if r0 == r1:

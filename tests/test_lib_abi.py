@@ -78,9 +78,9 @@ def test_argument_validation_without_gpu(pkg):
     assert lib.moe_fp8_ds_ep_combine(None, None, 0, 2, None, None) == L.MOE_OK
     assert lib.moe_fp8_ds_ep_combine(None, None, 4, 9, None, None) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_tile_override(0, 0) == L.MOE_OK
-    assert lib.moe_fp8_ds_set_path_override(4) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_set_path_override(3) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_set_path_override(-1) == L.MOE_ERR_INVALID_ARGUMENT
-    assert lib.moe_fp8_ds_set_path_override(3) == L.MOE_OK
+    assert lib.moe_fp8_ds_set_path_override(2) == L.MOE_OK
     assert lib.moe_fp8_ds_set_path_override(0) == L.MOE_OK
 
 
