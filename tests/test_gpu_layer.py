@@ -374,3 +374,28 @@ def test_no_local_rows_zero_output(pkg, oracle, cuda_dev):
     assert torch.count_nonzero(out.float()) == 0
     out2, _, _ = run_layer(pkg, d, ws=ws)
     assert torch.count_nonzero(out2.float()) == 0
+
+
+# ---------------------------------------------------------------------------- range
+@pytest.mark.parametrize("path", [1, 2])
+@pytest.mark.parametrize("hs_mult,w_mult", [(1e3, 1e2), (1e-4, 1.0), (1.0, 1e-3)])
+def test_scaled_inputs_keep_their_precision(path, hs_mult, w_mult, pkg, oracle, cuda_dev):
+    """Block scales far from 1 (the definition allows any fp32 scale): hidden
+    scales x1e3 with weight scales x1e2 (SwiGLU outputs far above the f16 range,
+    ~1e10), hidden scales x1e-4, weight scales x1e-3.  Both GEMM families keep
+    the layer's relative tolerance; the absolute term scales with the output."""
+    base = cached_inputs(96, 8, 0, 21)
+    inp = dict(base)
+    inp["hidden_states_scale"] = base["hidden_states_scale"] * hs_mult
+    inp["gemm1_weights_scale"] = base["gemm1_weights_scale"] * w_mult
+    inp["gemm2_weights_scale"] = base["gemm2_weights_scale"] * w_mult
+    ref0 = oracle.moe_forward(*pkg.inputs.as_args(base), return_fp32=True)
+    ref = oracle.moe_forward(*pkg.inputs.as_args(inp), return_fp32=True)
+    k = float(ref.abs().max() / ref0.abs().max())
+    out, _, _ = run_layer(pkg, to_dev(inp, cuda_dev), path=path)
+    got = out.float().cpu()
+    assert torch.isfinite(got).all()
+    d = (got - ref).abs()
+    bad = int((d > ATOL * k + RTOL * ref.abs()).sum())
+    print(f"path {path} hs x{hs_mult} w x{w_mult}: output scale {k:.3e}, max rel {float((d / ref.abs().clamp_min(1e-30)).max()):.3e}")
+    assert bad == 0, f"{bad} elements outside tolerance (max_abs {float(d.max()):.3e}, scale {k:.3e})"
