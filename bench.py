@@ -206,40 +206,69 @@ def stage_times(L, fn, steps, flush):
     return {s: statistics.mean(v) for s, v in per.items()}
 
 
-def e2e_steps(pkg, inp, T, steps, warmup):
-    """Public kernel(...) with the step's activations copied from pinned host memory
-    and the bf16 output read back, all inside the timed region (weights resident)."""
+def e2e_steps(pkg, inp, T, steps, warmup, pipelined=True):
+    """Public kernel(...) with each step's activations copied from pinned host
+    memory and its bf16 output read back, all inside the timed region (weights
+    resident, as model parameters are).
+
+    pipelined=True runs it the way a serving loop does: two input and output
+    buffer sets, host-to-device copies on one side stream and device-to-host
+    reads on another, so step i+1's inputs arrive and step i-1's output leaves
+    while step i computes; every step still moves its own bytes.  False runs
+    copy, compute and read back one after the other on one stream."""
     dev = inp["hidden_states"].device
     h_logits = inp["routing_logits"].cpu().pin_memory()
     h_hidden = inp["hidden_states"].view(torch.uint8).cpu().pin_memory()
     h_scale = inp["hidden_states_scale"].cpu().pin_memory()
-    h_out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
-    d_logits = torch.empty_like(inp["routing_logits"])
-    d_hidden = torch.empty(T, H, dtype=torch.uint8, device=dev)
-    d_scale = torch.empty_like(inp["hidden_states_scale"])
-    d_out = torch.empty(T, H, dtype=torch.bfloat16, device=dev)
+    nbuf = 2 if pipelined else 1
+    h_out = [torch.empty(T, H, dtype=torch.bfloat16).pin_memory() for _ in range(nbuf)]
+    d_logits = [torch.empty_like(inp["routing_logits"]) for _ in range(nbuf)]
+    d_hidden = [torch.empty(T, H, dtype=torch.uint8, device=dev) for _ in range(nbuf)]
+    d_scale = [torch.empty_like(inp["hidden_states_scale"]) for _ in range(nbuf)]
+    d_out = [torch.empty(T, H, dtype=torch.bfloat16, device=dev) for _ in range(nbuf)]
+    comp = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(dev) if pipelined else comp
+    s_out = torch.cuda.Stream(dev) if pipelined else comp
+    in_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    in_free = [torch.cuda.Event() for _ in range(nbuf)]
+    out_ready = [torch.cuda.Event() for _ in range(nbuf)]
+    out_free = [torch.cuda.Event() for _ in range(nbuf)]
 
-    def step():
-        d_logits.copy_(h_logits, non_blocking=True)
-        d_hidden.copy_(h_hidden, non_blocking=True)
-        d_scale.copy_(h_scale, non_blocking=True)
-        pkg.kernel(d_logits, inp["routing_bias"], d_hidden.view(torch.float8_e4m3fn), d_scale,
+    def step(i):
+        j = i % nbuf
+        with torch.cuda.stream(s_in):
+            s_in.wait_event(in_free[j])            # the kernel two steps back has read set j
+            d_logits[j].copy_(h_logits, non_blocking=True)
+            d_hidden[j].copy_(h_hidden, non_blocking=True)
+            d_scale[j].copy_(h_scale, non_blocking=True)
+            in_ready[j].record(s_in)
+        comp.wait_event(in_ready[j])
+        comp.wait_event(out_free[j])               # output set j has been read back
+        pkg.kernel(d_logits[j], inp["routing_bias"], d_hidden[j].view(torch.float8_e4m3fn), d_scale[j],
                    inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"],
-                   inp["gemm2_weights_scale"], inp["local_expert_offset"], inp["routed_scaling_factor"], d_out)
-        h_out.copy_(d_out, non_blocking=True)
+                   inp["gemm2_weights_scale"], inp["local_expert_offset"], inp["routed_scaling_factor"], d_out[j])
+        in_free[j].record(comp)
+        out_ready[j].record(comp)
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(out_ready[j])
+            h_out[j].copy_(d_out[j], non_blocking=True)
+            out_free[j].record(s_out)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(steps):
-        step()
-    b.record()
+    a.record(comp)
+    s_in.wait_event(a)
+    for i in range(steps):
+        step(i)
+    comp.wait_stream(s_out)                        # the last read-back is inside the region
+    comp.wait_stream(s_in)
+    b.record(comp)
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / steps
     h2d = h_logits.numel() * 4 + h_hidden.numel() + h_scale.numel() * 4
-    return ms, h2d, h_out.numel() * 2
+    return ms, h2d, h_out[0].numel() * 2
 
 
 def cpu_baseline(inp_dev, sample_s):
@@ -539,6 +568,7 @@ def main():
     dom = max(("gemm1", "gemm2"), key=lambda s: stages[s])
     achieved = ab[dom] / (stages[dom] * 1e-3) / 1e9
     e2e_ms, h2d, d2h = e2e_steps(pkg, inp, T, a.steps, a.warmup)
+    e2e_serial_ms, _, _ = e2e_steps(pkg, inp, T, a.steps, a.warmup, pipelined=False)
 
     sweep = []
     for Ts, skewed in sweep_T:
@@ -603,7 +633,10 @@ def main():
         "sweep": sweep,
         "cpu_baseline": cpu,
         "e2e": {"value": T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "mode": "pipelined: inputs of step i+1 copied in and output of step i-1 read back while "
+                        "step i computes (two buffer sets, two copy streams)",
+                "serial_ms_per_step": e2e_serial_ms},
         "clocks": clocks,
         "gpu_launches": a.steps * L.load().moe_fp8_ds_launches_per_call(T),
     }
