@@ -60,6 +60,8 @@ def parse_args():
                    help="extra T values ('' for none); a trailing 's' marks the skewed stress batch")
     p.add_argument("--local-experts", type=int, default=32)
     p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--path", type=int, default=0,
+                   help="GEMM family: 0 automatic, 1 weights-on-M, 2 tokens-on-M (moe_fp8_ds_set_path_override)")
     p.add_argument("--cpu-sample-s", type=float, default=12.0)
     return p.parse_args()
 
@@ -541,6 +543,7 @@ def main():
     K = sys.modules["fib_b200.kernel"]
     L = sys.modules["fib_b200._lib"]
     hbm_peak, peak_kind = measured_peaks()
+    L.check(L.load().moe_fp8_ds_set_path_override(a.path), "moe_fp8_ds_set_path_override")
 
     sweep_T = parse_sweep(a.sweep)
     base = pkg.inputs.bench_batch(max(BENCH_BASE_TOKENS, T), device=dev) if E_l == 32 else \
