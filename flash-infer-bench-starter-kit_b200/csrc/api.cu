@@ -297,7 +297,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     const uint32_t ks1 = (uint32_t)gemm_tm_k_per_stage(1), ks2 = (uint32_t)gemm_tm_k_per_stage(2);
     if (!encode_kmajor_planes(&tm_w1, a->gemm1_weights, kHidden, kInter, 2ull * E_l, 128, ks1) ||
         !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, 128, ks1) ||
-        !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 256, ks2) ||
+        !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
         !encode_kmajor_planes(&tm_b2, inter, kInter, (uint64_t)P.R_cap, 2, 128, ks2))
       return MOE_ERR_INVALID_ARGUMENT;
     // token scales [K blocks][R_cap]: boxes of 132 rows x the stage's K blocks;
@@ -308,7 +308,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     if (!encode_f32_2d(&tm_bs1, act_scale, (uint64_t)P.R_cap, kHiddenBlocks, sbox, ks1) ||
         !encode_f32_2d(&tm_bs2, inter_scale, (uint64_t)P.R_cap, kInterBlocks, sbox, ks2) ||
         !encode_f32_3d(&tm_ws1, a->gemm1_weights_scale, kHiddenBlocks, kInter / 128, 2ull * E_l, 4, 1, 2) ||
-        !encode_f32_3d(&tm_ws2, a->gemm2_weights_scale, kInterBlocks, kHidden / 128, (uint64_t)E_l, 4, 2, 1))
+        !encode_f32_3d(&tm_ws2, a->gemm2_weights_scale, kInterBlocks, kHidden / 128, (uint64_t)E_l, 4, 1, 1))
       return MOE_ERR_INVALID_ARGUMENT;
   } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);

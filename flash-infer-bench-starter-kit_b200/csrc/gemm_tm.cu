@@ -19,17 +19,18 @@
 // requantisation never leave the SM.  c is stored as two e4m3 terms on the
 // same scale s = amax/448, c ~= (hi + lo)*s, hi in plane 0 and lo in plane 1
 // of the intermediate [2][R_cap][2048].
-// GEMM2 (KIND 2, 2048 -> 7168): halves A and B are hidden rows 256n.. and
-// 256n+128..; each K block runs two MMAs per half into the same partial, one
-// with the hi plane and one with the lo plane (they share the scale s), so the
-// two-term intermediate costs MMA time but no extra promotion.
+// GEMM2 (KIND 2, 2048 -> 7168): a unit is 128 tokens x 128 hidden rows; each
+// K block runs two MMAs into the same partial, one with the hi plane and one
+// with the lo plane (they share the scale s), so the two-term intermediate
+// costs MMA time but no extra promotion.
 //
-// TMEM holds two K-block partials of the whole unit (2 x 256 columns of 128
-// lanes), so the tensor core computes K block k+1 while the epilogue warps
-// promote K block k.  The running accumulators live in registers: each of the
-// 256 epilogue threads owns one token row (its TMEM lane) and 64 columns of
-// each half, 128 fp32 values (hence two warpgroups and 168 registers per
-// thread; a block of 10 warps leaves that many).
+// TMEM holds NSLOT K-block partials of a whole unit (GEMM1 2 x 256 columns,
+// GEMM2 4 x 128), so the tensor core runs one (three) K blocks ahead of the
+// epilogue warps promoting the oldest one.  The running accumulators live in
+// registers: each of the 256 epilogue threads owns one token row (its TMEM
+// lane) and 64 columns of each half (GEMM1: 128 fp32 values, hence two
+// warpgroups and 168 registers per thread; a block of 10 warps leaves that
+// many).
 //
 // Pipeline: TMA producer (warp 8) -> STAGES-deep ring of {token tile(s), two
 // weight tiles, their block scales} per K step -> MMA issuer (warp 9, also
@@ -52,13 +53,18 @@ struct TmCfg {
   static constexpr int K = KIND == 1 ? kHidden : kInter;
   static constexpr int KB = K / 128;                        // 128-wide K blocks
   static constexpr int KSTEPS = KB / KS;                    // pipeline iterations per unit
-  static constexpr int NT = KIND == 1 ? kInter / 128 : kHidden / 256;   // units per token tile
+  // Output columns of a unit: NH halves of 128 (GEMM1: X1 and X2 of 128
+  // features, so SwiGLU and the 1x128 requantisation stay in one unit; GEMM2:
+  // 128 hidden rows).  TMEM holds NSLOT K-block partials of a whole unit.
+  static constexpr int NH = KIND == 1 ? 2 : 1;
+  static constexpr int NSLOT = 512 / (NH * 128);
+  static constexpr int NT = KIND == 1 ? kInter / 128 : kHidden / 128;   // units per token tile
   static constexpr int W_ROWS = KIND == 1 ? kGemm1Out : kHidden;        // weight rows per expert
   static constexpr int NA = KIND == 1 ? 1 : 2;              // token tiles per K block (GEMM2: hi, lo)
   static constexpr int TILE = 128 * 128;                    // one [128 rows x 128 B] operand tile
   static constexpr int OFF_WA = KS * NA * TILE;             // weight tiles inside a stage
   static constexpr int OFF_WB = OFF_WA + KS * TILE;
-  static constexpr int STAGE = OFF_WB + KS * TILE;
+  static constexpr int STAGE = OFF_WA + NH * KS * TILE;
   static constexpr int NEPI = 256;                          // two epilogue warpgroups (warps 0..7)
   static constexpr int W_PROD = 8, W_MMA = 9;               // producer and MMA warps
   static constexpr int THREADS = NEPI + 64;
@@ -74,14 +80,14 @@ struct TmCfg {
   static constexpr int SC_ROW = 132;
   static constexpr int SC_ACT = KS * SC_ROW * 4;
   static constexpr int SC_SLOT = ((SC_ACT + 127) / 128) * 128 + 128;
-  static constexpr int SC_TX = SC_ACT + 2 * 4 * 4;
+  static constexpr int SC_TX = SC_ACT + NH * 4 * 4;
   static constexpr int OFF_SC = 2048 + 2 * 2 * 128 * 4;    // after barriers + amax exchange [2][2][128]
   static constexpr int AUX = OFF_SC + SR * SC_SLOT;
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
   static_assert(KS == 1 || KS == 2 || KS == 4, "weight-scale boxes cover 4 aligned K blocks");
-  static_assert(KIND == 1 || KS == 1, "GEMM2's 256-row weight box holds one K block");
-  static constexpr uint32_t SLOT_COLS = 256, P_B = 128;     // partial slot: half A at +0, half B at +128
-  static constexpr int PART_FLOATS = 128 * 256;             // one published share: [128 rows][256 cols]
+  static constexpr uint32_t SLOT_COLS = NH * 128, P_B = 128;   // partial slot: half A at +0, half B at +128
+  static constexpr int PART_COLS = NH * 128;
+  static constexpr int PART_FLOATS = 128 * 256;             // one published share slot: [128 rows][<= 256 cols]
   static_assert(KB % KS == 0, "K steps");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
@@ -97,9 +103,9 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
   uint8_t* aux = smem + STAGES * C::STAGE;
   uint64_t* full = reinterpret_cast<uint64_t*>(aux);        // TMA bytes of stage s landed
   uint64_t* empty = full + STAGES;                          // MMAs finished reading stage s
-  uint64_t* pfull = empty + STAGES;                         // [2] partial slot written
-  uint64_t* pempty = pfull + 2;                             // [2] partial slot read
-  uint64_t* sfull = pempty + 2;                             // [SR] scales of an iteration landed
+  uint64_t* pfull = empty + STAGES;                         // [NSLOT] partial slot written
+  uint64_t* pempty = pfull + C::NSLOT;                      // [NSLOT] partial slot read
+  uint64_t* sfull = pempty + C::NSLOT;                      // [SR] scales of an iteration landed
   uint64_t* sempty = sfull + C::SR;                         // [SR] scales read by every epilogue warp
   uint64_t* drain = sempty + C::SR;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
@@ -120,7 +126,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
     for (int s = 0; s < C::SR; ++s) { mbar_init(&sfull[s], 1); mbar_init(&sempty[s], C::NEPI / 32); }
-    for (int h = 0; h < 2; ++h) { mbar_init(&pfull[h], 1); mbar_init(&pempty[h], C::NEPI / 32); }
+    for (int h = 0; h < C::NSLOT; ++h) { mbar_init(&pfull[h], 1); mbar_init(&pempty[h], C::NEPI / 32); }
     mbar_init(drain, 1);
     *const_cast<int*>(abort_flag) = 0;
     fence_mbar_init();
@@ -157,13 +163,13 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         // Two operand boxes per stage (fewer, larger TMA boxes stream faster):
         // GEMM1 tokens {128 B, 128 rows, KS} + weights {128 B, 128 rows, KS,
         // X1|X2} (W13 viewed as [2E_l][56][2048][128 B]); GEMM2 tokens {128 B,
-        // 128 rows, KS, hi|lo} + weights {128 B, 256 rows, KS}.
+        // 128 rows, KS, hi|lo} + weights {128 B, 128 rows, KS}.
         if (KIND == 1) {
           tma_load_3d(&tm_b, &full[s], st, 0, tile.y, z, pol_b);
           tma_load_4d(&tm_w, &full[s], st + C::OFF_WA, 0, mn.y * 128, z, 2 * tile.x, pol_w);
         } else {
           tma_load_4d(&tm_b, &full[s], st, 0, tile.y, z, 0, pol_b);
-          tma_load_3d(&tm_w, &full[s], st + C::OFF_WA, 0, tile.x * C::W_ROWS + mn.y * 256, z, pol_w);
+          tma_load_3d(&tm_w, &full[s], st + C::OFF_WA, 0, tile.x * C::W_ROWS + mn.y * 128, z, pol_w);
         }
         ++issued;
         // this iteration's block scales into scale slot i % SR
@@ -175,7 +181,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         if (KIND == 1)   // w_scale viewed as {56 K blocks, 16 n-blocks, 2 halves x E_l}
           tma_load_3d(&tm_ws, &sfull[q], sc + C::SC_SLOT - 128, z & ~3, mn.y, 2 * tile.x, pol_b);
         else             // w_scale viewed as {16 K blocks, 56 n-blocks, E_l}
-          tma_load_3d(&tm_ws, &sfull[q], sc + C::SC_SLOT - 128, z & ~3, 2 * mn.y, tile.x, pol_b);
+          tma_load_3d(&tm_ws, &sfull[q], sc + C::SC_SLOT - 128, z & ~3, mn.y, tile.x, pol_b);
         ++sissued;
       }
       if (!ok) {
@@ -198,7 +204,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
       const uint32_t smem_base = smem_u32(smem);
       constexpr uint32_t idesc = make_idesc_f8(128, 128);
       bool ok = true;
-      int g = 0;                       // K blocks issued so far (slot g & 1, phase (g >> 1) & 1)
+      int g = 0;                       // K blocks issued so far (slot g % NSLOT, phase (g / NSLOT) & 1)
       for (int i = 0; i < n_iter && ok; ++i) {
         const int s = i % STAGES;
         if (!mbar_wait_bounded(&full[s], (i / STAGES) & 1, abort_flag)) { ok = false; break; }
@@ -206,11 +212,11 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         const uint32_t st = smem_base + s * C::STAGE;
 #pragma unroll 1
         for (int kk = 0; kk < KS; ++kk, ++g) {
-          const int slot = g & 1;
-          if (!mbar_wait_bounded(&pempty[slot], ((g >> 1) & 1) ^ 1, abort_flag)) { ok = false; break; }
+          const int slot = g % C::NSLOT;
+          if (!mbar_wait_bounded(&pempty[slot], ((g / C::NSLOT) & 1) ^ 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < C::NH; ++h) {
             const uint64_t bdesc = make_sdesc_sw128(st + (h ? C::OFF_WB : C::OFF_WA) + kk * C::TILE);
             const uint32_t d = tmem_base + slot * C::SLOT_COLS + (h ? C::P_B : 0u);
 #pragma unroll
@@ -240,8 +246,8 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     const uint32_t lane_addr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(wg * C::COLS);
     const int col0 = wg * C::COLS;
 
-    float acc[2][C::COLS];                      // running sums: [half][column]
-    int g = 0;                                  // K blocks consumed (slot g & 1)
+    float acc[C::NH][C::COLS];                  // running sums: [half][column]
+    int g = 0;                                  // K blocks consumed (slot g % NSLOT)
     int seg_k0 = 0;
     int nseg = 0;                               // segments finished (amax buffer parity)
     int4 tile = make_int4(0, 0, 0, 0);
@@ -259,7 +265,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         row_ok = j < tile.z;
         seg_k0 = ks;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < C::NH; ++h)
 #pragma unroll
           for (int x = 0; x < C::COLS; ++x) acc[h][x] = 0.f;
       }
@@ -275,25 +281,25 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
           const float as = row_ok ? sc[kk * C::SC_ROW + (tile.y & 3) + j] : 0.f;
           const int x = (ks * KS + kk) & 3;
           cA[kk] = as * wsc[x];
-          cB[kk] = as * wsc[4 + x];
+          cB[kk] = C::NH > 1 ? as * wsc[4 + x] : 0.f;
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&sempty[sq]);
       }
 #pragma unroll
       for (int kk = 0; kk < KS && !aborted; ++kk, ++g) {
-        const int slot = g & 1;
-        if (!mbar_wait_warp(&pfull[slot], (g >> 1) & 1, abort_flag)) { aborted = true; break; }
+        const int slot = g % C::NSLOT;
+        if (!mbar_wait_warp(&pfull[slot], (g / C::NSLOT) & 1, abort_flag)) { aborted = true; break; }
         tc_fence_after();
         const uint32_t pbase = lane_addr + slot * C::SLOT_COLS;
-        // 8 chunks of 16 columns (4 per half), two loads in flight
+        // 4*NH chunks of 16 columns (4 per half), two loads in flight
 #pragma unroll
-        for (int cc = 0; cc < 8; cc += 2) {
+        for (int cc = 0; cc < 4 * C::NH; cc += 2) {
           float pv[2][16];
           tmem_ld16(pbase + (cc >> 2) * C::P_B + (cc & 3) * 16, pv[0]);
           tmem_ld16(pbase + ((cc + 1) >> 2) * C::P_B + ((cc + 1) & 3) * 16, pv[1]);
           tmem_ld_wait();
-          if (cc == 6) {                        // every load of this slot is done: release it
+          if (cc == 4 * C::NH - 2) {            // every load of this slot is done: release it
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&pempty[slot]);
@@ -319,9 +325,9 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         // stream-K: publish this share, the last contributor adds all of them
         // in ascending CTA order (its own share included, re-read)
         float* mine = p.partials + (size_t)(blockIdx.x * 2 + sch.slot(blockIdx.x, r, C::KSTEPS)) * C::PART_FLOATS +
-                      (size_t)j * 256 + col0;
+                      (size_t)j * C::PART_COLS + col0;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < C::NH; ++h)
 #pragma unroll
           for (int w = 0; w < C::COLS / 4; ++w)
             __stcg(reinterpret_cast<float4*>(mine + h * 128) + w,
@@ -338,14 +344,14 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         if (!last_flag[0]) continue;
         __threadfence();
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+        for (int h = 0; h < C::NH; ++h)
 #pragma unroll
           for (int x = 0; x < C::COLS; ++x) acc[h][x] = 0.f;
         for (int c = c_lo; c <= c_hi; ++c) {
           const float* src = p.partials + (size_t)(c * 2 + sch.slot(c, r, C::KSTEPS)) * C::PART_FLOATS +
-                             (size_t)j * 256 + col0;
+                             (size_t)j * C::PART_COLS + col0;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < C::NH; ++h)
 #pragma unroll
             for (int w = 0; w < C::COLS / 4; ++w) {
               const float4 f = __ldcg(reinterpret_cast<const float4*>(src + h * 128) + w);
@@ -362,7 +368,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         float m = 0.f;
 #pragma unroll
         for (int x = 0; x < C::COLS; ++x) {
-          const float x2 = acc[1][x];
+          const float x2 = acc[C::NH - 1][x];
           acc[0][x] = x2 * __frcp_rn(1.0f + __expf(-x2)) * acc[0][x];
           m = fmaxf(m, fabsf(acc[0][x]));
         }
@@ -401,8 +407,8 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
         if (row_ok && wg == 0) p.inter_scale[(size_t)nt * p.R_cap + row] = sc;
       } else if (row_ok) {
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          float4* d = reinterpret_cast<float4*>(p.down + row * kHidden + nt * 256 + h * 128 + col0);
+        for (int h = 0; h < C::NH; ++h) {
+          float4* d = reinterpret_cast<float4*>(p.down + row * kHidden + nt * (C::NH * 128) + h * 128 + col0);
 #pragma unroll
           for (int w = 0; w < C::COLS / 4; ++w)
             d[w] = make_float4(acc[h][4 * w], acc[h][4 * w + 1], acc[h][4 * w + 2], acc[h][4 * w + 3]);
@@ -427,7 +433,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
 // --------------------------------------------------------------------------
 template <int KIND> struct TmPick;   // K blocks per stage, stages
 template <> struct TmPick<1> { static constexpr int KS = 1, S = 4; };
-template <> struct TmPick<2> { static constexpr int KS = 1, S = 3; };
+template <> struct TmPick<2> { static constexpr int KS = 1, S = 4; };
 
 template <int KIND>
 using TmCfgOf = TmCfg<KIND, TmPick<KIND>::KS, TmPick<KIND>::S>;
