@@ -87,6 +87,8 @@ struct TmCfg {
   static_assert(KS == 1 || KS == 2 || KS == 4, "weight-scale boxes cover 4 aligned K blocks");
   static constexpr uint32_t SLOT_COLS = NH * 128, P_B = 128;   // partial slot: half A at +0, half B at +128
   static constexpr int PART_COLS = NH * 128;
+  // GEMM1 with one K block per stage: both weight halves form one N = 256 operand
+  static constexpr bool WIDE = KIND == 1 && KS == 1;
   static constexpr int PART_FLOATS = 128 * 256;             // one published share slot: [128 rows][<= 256 cols]
   static_assert(KB % KS == 0, "K steps");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -203,6 +205,7 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
     if (elect_one_lane()) {
       const uint32_t smem_base = smem_u32(smem);
       constexpr uint32_t idesc = make_idesc_f8(128, 128);
+      constexpr uint32_t idesc_wide = make_idesc_f8(128, 256);
       bool ok = true;
       int g = 0;                       // K blocks issued so far (slot g % NSLOT, phase (g / NSLOT) & 1)
       for (int i = 0; i < n_iter && ok; ++i) {
@@ -215,16 +218,28 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
           const int slot = g % C::NSLOT;
           if (!mbar_wait_bounded(&pempty[slot], ((g / C::NSLOT) & 1) ^ 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
+          if (C::WIDE) {
+            // GEMM1: the X1 and X2 weight tiles sit back to back (rows 0..255 of
+            // one K-major operand), so one N = 256 MMA per K slice fills both
+            // halves of the partial and the token tile is read once, not twice.
+            const uint64_t adesc = make_sdesc_sw128(st + kk * C::TILE);
+            const uint64_t bdesc = make_sdesc_sw128(st + C::OFF_WA);
+            const uint32_t d = tmem_base + slot * C::SLOT_COLS;
 #pragma unroll
-          for (int h = 0; h < C::NH; ++h) {
-            const uint64_t bdesc = make_sdesc_sw128(st + (h ? C::OFF_WB : C::OFF_WA) + kk * C::TILE);
-            const uint32_t d = tmem_base + slot * C::SLOT_COLS + (h ? C::P_B : 0u);
+            for (int k = 0; k < 4; ++k)   // 4 x K=32 per 128-byte K block; +32 B = +2 in addr>>4
+              tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc_wide, k == 0 ? 0u : 1u);
+          } else {
 #pragma unroll
-            for (int a = 0; a < C::NA; ++a) {
-              const uint64_t adesc = make_sdesc_sw128(st + (a * KS + kk) * C::TILE);
+            for (int h = 0; h < C::NH; ++h) {
+              const uint64_t bdesc = make_sdesc_sw128(st + (h ? C::OFF_WB : C::OFF_WA) + kk * C::TILE);
+              const uint32_t d = tmem_base + slot * C::SLOT_COLS + (h ? C::P_B : 0u);
 #pragma unroll
-              for (int k = 0; k < 4; ++k)   // 4 x K=32 per 128-byte K block; +32 B = +2 in addr>>4
-                tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc, (a == 0 && k == 0) ? 0u : 1u);
+              for (int a = 0; a < C::NA; ++a) {
+                const uint64_t adesc = make_sdesc_sw128(st + (a * KS + kk) * C::TILE);
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                  tc_mma_f8(d, adesc + 2 * k, bdesc + 2 * k, idesc, (a == 0 && k == 0) ? 0u : 1u);
+              }
             }
           }
           tc_commit(&pfull[slot]);
