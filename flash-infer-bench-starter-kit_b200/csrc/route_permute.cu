@@ -472,13 +472,19 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   griddep_wait();
-  // GEMM1 is released only after the grid barrier below, so it cannot see the
-  // previous call's flags: they are cleared here, before CTA 0 reaches it.
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
+  // GEMM1 is released only after the barrier below, so it cannot see the
+  // previous call's flags: they are cleared (and fenced) before CTA 0 reaches
+  // it, by a warp of CTA 0 that routes no token when there is one (the fence
+  // then stays off the routing path), else by warp 0 after its token.
+  const bool single = gridDim.x == 1;
+  const int reset_warp = T < kRouteTokens ? kRouteTokens - 1 : 0;
+  const bool resetter = blockIdx.x == 0 && threadIdx.x == reset_warp * 32;
+  auto reset_flags = [&]() {
     front_sync[0] = 0;
     front_sync[1] = 0;
     __threadfence();
-  }
+  };
+  if (resetter && T < kRouteTokens) reset_flags();
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) s_mask[e] = 0;
   if (threadIdx.x == 0) s_n = 0;
   __syncthreads();
@@ -492,15 +498,18 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
       if (le >= 0 && le < E_l) atomicOr(&s_mask[le], 1u << warp);
     }
   }
+  if (resetter && T >= kRouteTokens) reset_flags();
   __syncthreads();
-  store_masks(masks8, NB8p, E_l, s_mask);
+  if (!single) store_masks(masks8, NB8p, E_l, s_mask);
   // Up to eight CTAs run as one thread-block cluster (launch attribute) and
   // meet at the hardware cluster barrier, which also orders their global
   // writes (release/acquire at cluster scope); larger grids use the bounded
   // software grid barrier.
   uint32_t nctas_in_cluster;
   asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(nctas_in_cluster));
-  if (nctas_in_cluster == gridDim.x && gridDim.x > 1) {
+  if (single) {
+    // one CTA: the masks stay in shared memory, no barrier beyond the block's
+  } else if (nctas_in_cluster == gridDim.x) {
     __syncthreads();
     asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
   } else if (!grid_barrier(err + 1, err + 2, err)) {
@@ -511,10 +520,10 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
   for (int e = threadIdx.x; e < E_l; e += blockDim.x) {
     const unsigned int* row = reinterpret_cast<const unsigned int*>(masks8 + (size_t)e * NB8p);
     const int g0 = blockIdx.x;
-    int before = 0, total = 0;
+    int before = 0, total = single ? __popc(s_mask[e]) : 0;
 #pragma unroll
     for (int q = 0; q < kFrontMaxTokens / kPermBlock; ++q) {
-      if (q * 4 >= NB8p) break;
+      if (single || q * 4 >= NB8p) break;
       const uint32_t m = __ldcg(row + q);
       total += __popc(m);
       if (4 * q + 4 <= g0) before += __popc(m);
