@@ -185,14 +185,23 @@ def run_with_workspace(args: _lib.MoeArgs, ws: torch.Tensor, stream: int | None 
 def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
            gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
            local_expert_offset, routed_scaling_factor, output):
-    """Fused FP8 block-scale MoE forward with DeepSeek-V3 routing (DPS: writes ``output``)."""
+    """Fused FP8 block-scale MoE forward with DeepSeek-V3 routing (DPS: writes ``output``).
+
+    The call may be captured in a CUDA graph (``torch.cuda.graph``): make one
+    eager call on the capturing stream first, so its workspace exists before
+    the capture; replays then rerun the same launches on the same buffers."""
     args = build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                       local_expert_offset, routed_scaling_factor, output)
     with torch.cuda.device(hidden_states.device):
         ent = _entry(hidden_states.device, workspace_bytes(args.num_tokens, args.num_local_experts))
         run_with_workspace(args, ent.buf)
-        ent.event.record()
+        # Under CUDA-graph capture the launches become graph nodes and the
+        # last-use event is not recorded (an event recorded in a capture cannot
+        # be waited on outside it); synchronise the replay stream before
+        # read_device_error after replays.
+        if not torch.cuda.is_current_stream_capturing():
+            ent.event.record()
 
 
 def read_device_error(device: torch.device | None = None) -> int:

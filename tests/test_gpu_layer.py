@@ -321,6 +321,42 @@ def test_streams_get_their_own_workspace(pkg, cuda_dev):
     assert K.read_device_error(cuda_dev) == 0
 
 
+def test_cuda_graph_capture_replays_bitwise(pkg, cuda_dev):
+    """kernel(...) captured in a CUDA graph: replays on new inputs copied into the
+    captured buffers equal eager calls on those inputs, bit for bit, for a decode
+    batch (fused front kernel) and a prefill batch (tokens-on-M GEMMs)."""
+    K, _ = _mods()
+    for T, E_l, seeds in ((64, 32, (13, 14)), (2048, 8, (21, 22))):
+        inputs = [to_dev(cached_inputs(T, E_l, 0, sd), cuda_dev) for sd in seeds]
+        want = []
+        for inp in inputs:
+            out = torch.empty(T, 7168, dtype=torch.bfloat16, device=cuda_dev)
+            pkg.kernel(*pkg.inputs.as_args(inp), out)
+            want.append(out)
+        buf = {k: (v.clone() if torch.is_tensor(v) else v) for k, v in inputs[0].items()}
+        out = torch.empty(T, 7168, dtype=torch.bfloat16, device=cuda_dev)
+        s = torch.cuda.Stream(cuda_dev)
+        s.wait_stream(torch.cuda.current_stream(cuda_dev))
+        with torch.cuda.stream(s):
+            pkg.kernel(*pkg.inputs.as_args(buf), out)   # workspace of the capture stream
+        torch.cuda.current_stream(cuda_dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            pkg.kernel(*pkg.inputs.as_args(buf), out)
+        for _ in range(2):
+            for inp, ref in zip(inputs, want):
+                for k in buf:
+                    if torch.is_tensor(buf[k]):
+                        buf[k].copy_(inp[k])
+                    else:
+                        assert buf[k] == inp[k]
+                out.fill_(float("nan"))
+                g.replay()
+                torch.cuda.synchronize(cuda_dev)
+                assert torch.equal(out.view(torch.int16), ref.view(torch.int16)), f"graph replay differs (T={T})"
+        assert K.read_device_error(cuda_dev) == 0
+
+
 def test_routed_entry_equals_full_entry(pkg, cuda_dev):
     K, L = _mods()
     inp = to_dev(cached_inputs(64, 32, 0, 13), cuda_dev)
