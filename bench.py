@@ -346,25 +346,38 @@ def run_ep(a, world, rank, local_rank):
     T_l = EP_TOKENS // world
     logits, bias, hs, hss = pkg.inputs.make_token_inputs(T_l, seed=1000 + rank, device=dev)
     w13, s13, w2, s2 = pkg.inputs.make_expert_shard(rank * E_l, E_l, seed=0, device=dev)
-    layer = ep.from_library()
+    # Fixed per-peer capacity (every rank brings T_l tokens): no device-to-host
+    # synchronisation inside a step.  The exact-count variant (row counts read
+    # on the host every step) is timed beside it.
+    layer = ep.from_library(capacity=T_l)
+    layer_exact = ep.from_library()
     out = torch.empty(T_l, H, dtype=torch.bfloat16, device=dev)
+
+    def timed(lay, clk=None):
+        f = lambda: lay(logits, bias, hs, hss, w13, s13, w2, s2, 2.5, out)  # noqa: E731
+        for _ in range(a.warmup):
+            f()
+        dist.barrier()
+        torch.cuda.synchronize()
+        if clk is not None:
+            clk.__enter__()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            f()
+        e1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        if clk is not None:
+            clk.__exit__(None, None, None)
+        t = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t)
+    clk = ClockSampler(local_rank)
+    ms = timed(layer, clk)
+    ms_exact = timed(layer_exact)
     fn = lambda: layer(logits, bias, hs, hss, w13, s13, w2, s2, 2.5, out)  # noqa: E731
-    for _ in range(a.warmup):
-        fn()
-    dist.barrier()
-    torch.cuda.synchronize()
-    clk = ClockSampler(local_rank).__enter__()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    ev0.record()
-    for _ in range(a.steps):
-        fn()
-    ev1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    clk.__exit__(None, None, None)
-    ms = torch.tensor([ev0.elapsed_time(ev1) / a.steps], device=dev)
-    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-    ms = float(ms)
     # e2e: token inputs from pinned host memory, output read back, inside the timed region
     h_in = [t.cpu().pin_memory() for t in (logits, hs.view(torch.uint8), hss)]
     d_in = [torch.empty_like(t, device=dev) for t in h_in]
@@ -408,13 +421,15 @@ def run_ep(a, world, rank, local_rank):
             "dtype": "fp8e4m3 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"ep_T{EP_TOKENS}_E256", "tokens_total": EP_TOKENS, "tokens_per_rank": T_l,
                        "experts_per_rank": E_l, "parallelism": f"ep{world}",
-                       "collectives": "NCCL all-to-all (counts, dispatch rows, fp32 partials)",
+                       "collectives": "NCCL all-to-all of fixed size (dispatch rows, fp32 partials; per-peer "
+                           "capacity = tokens per rank, padding rows, no host synchronisation)",
                        "l2": "inputs larger than L2 (weights %.1f GB per rank)" % (E_l * 44.05e-3),
                        "rank0_sent_rows": stats.get("sent_rows"), "rank0_recv_rows": stats.get("recv_rows")},
             "e2e": {"value": EP_TOKENS / (float(e2e_ms) * 1e-3), "unit": "tokens/s",
                     "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in h_in) * world,
                     "d2h_bytes_per_step": h_out.numel() * 2 * world, "ms_per_step": float(e2e_ms)},
             "phase_ms_max_over_ranks": phases,
+            "exact_counts_ms_per_step": ms_exact,
             "clocks": clk.summary(),
             "gpu_launches": a.steps * 11,   # route, plan, pack, unpack, the routed layer (6), combine
         }

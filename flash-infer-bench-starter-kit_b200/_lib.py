@@ -61,6 +61,7 @@ EXPORTS = (
     "moe_fp8_ds_status_string", "moe_fp8_ds_launches_per_call", "moe_fp8_ds_set_tile_override",
     "moe_fp8_ds_set_stage_events", "moe_fp8_ds_run_noalloc", "moe_fp8_ds_set_path_override",
     "moe_fp8_ds_ep_plan", "moe_fp8_ds_ep_pack", "moe_fp8_ds_ep_unpack", "moe_fp8_ds_ep_combine",
+    "moe_fp8_ds_ep_plan_capacity", "moe_fp8_ds_ep_pack_capacity",
     "moe_fp8_ds_selftest_wait_timeout", "moe_fp8_ds_noalloc_read_device_error",
     "moe_fp8_ds_last_cuda_error_string",
 )
@@ -106,6 +107,8 @@ def load() -> ctypes.CDLL:
         lib.moe_fp8_ds_ep_pack.argtypes = [P, P, P, P, I32, P, I32, P, P]
         lib.moe_fp8_ds_ep_unpack.argtypes = [P, I32, P, P, P, P, P]
         lib.moe_fp8_ds_ep_combine.argtypes = [P, P, I32, I32, P, P]
+        lib.moe_fp8_ds_ep_plan_capacity.argtypes = [P, I32, I32, I32, I32, P, P, P, P]
+        lib.moe_fp8_ds_ep_pack_capacity.argtypes = [P, P, P, P, I32, P, I32, I32, I32, P, P]
         lib.moe_fp8_ds_selftest_wait_timeout.argtypes = [P, P]
         for name in EXPORTS:
             if name not in ("moe_fp8_ds_status_string", "moe_fp8_ds_last_cuda_error_string"):

@@ -23,9 +23,12 @@ constexpr int kMaxWorld = 8;
 
 // One CTA.  Pass 1 counts the rows each rank receives; pass 2 gives every
 // (token, rank) pair its send row: rank base + rank of the token among that
-// rank's tokens.
+// rank's tokens.  Compact layout (cap = 0): rank bases are the prefix sums of
+// the counts.  Fixed-capacity layout (cap >= T): rank r's rows start at
+// r * cap and the unused rows of its block are padding (src_token = -1), so
+// every all-to-all moves cap rows per peer and no count leaves the device.
 __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict__ ids, int T, int world,
-                                                        int experts_per_rank, int64_t* __restrict__ counts,
+                                                        int experts_per_rank, int cap, int64_t* __restrict__ counts,
                                                         int32_t* __restrict__ slot, int32_t* __restrict__ src_token) {
   __shared__ int s_warp[32][kMaxWorld];
   __shared__ int s_run[kMaxWorld];
@@ -56,12 +59,15 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
   if (tid == 0) {
     int acc = 0;
     for (int r = 0; r < world; ++r) {
-      s_base[r] = acc;
+      s_base[r] = cap > 0 ? r * cap : acc;
       counts[r] = s_run[r];
       acc += s_run[r];
     }
   }
   __syncthreads();
+  if (cap > 0)   // padding rows of every rank's block
+    for (int r = 0; r < world; ++r)
+      for (int j = s_run[r] + tid; j < cap; j += blockDim.x) src_token[r * cap + j] = -1;
   if (tid < kMaxWorld) s_run[tid] = 0;
   __syncthreads();
   // pass 2: slots, in token order inside each rank
@@ -103,14 +109,27 @@ __global__ void __launch_bounds__(1024) ep_plan_kernel(const int32_t* __restrict
   }
 }
 
+// A padding row (src_token < 0, fixed-capacity layout) is zero, with all 8
+// expert ids set to the first expert of the next rank: a valid id that the
+// receiving rank (row / cap) does not own, so its layer gives the row no work
+// and a zero partial.
 __global__ void __launch_bounds__(256) ep_pack_kernel(const int32_t* __restrict__ ids, const float* __restrict__ w,
                                                        const uint8_t* __restrict__ hidden,
                                                        const float* __restrict__ hidden_scale, int T,
-                                                       const int32_t* __restrict__ src_token,
-                                                       uint8_t* __restrict__ send) {
+                                                       const int32_t* __restrict__ src_token, int cap, int world,
+                                                       int experts_per_rank, uint8_t* __restrict__ send) {
   const int row = blockIdx.x;
   const int t = __ldg(src_token + row);
   uint8_t* dst = send + (size_t)row * kRowBytes;
+  if (t < 0) {
+    const int foreign = ((row / cap + 1) % world) * experts_per_rank;
+    for (int j = threadIdx.x; j < kOffIds / 16; j += blockDim.x)
+      reinterpret_cast<uint4*>(dst)[j] = make_uint4(0u, 0u, 0u, 0u);
+    const int j = threadIdx.x;
+    if (j < kTopK) reinterpret_cast<int32_t*>(dst + kOffIds)[j] = foreign;
+    else if (j < 2 * kTopK) reinterpret_cast<float*>(dst + kOffW)[j - kTopK] = 0.f;
+    return;
+  }
   const uint4* src = reinterpret_cast<const uint4*>(hidden + (size_t)t * kHidden);
   for (int j = threadIdx.x; j < kHidden / 16; j += blockDim.x)
     reinterpret_cast<uint4*>(dst)[j] = __ldg(src + j);
@@ -186,7 +205,20 @@ MOE_API int moe_fp8_ds_ep_plan(const int32_t* topk_ids, int32_t num_tokens, int3
     return MOE_ERR_INVALID_ARGUMENT;
   if (num_tokens > 0 && (!topk_ids || !slot || !src_token)) return MOE_ERR_INVALID_ARGUMENT;
   ep_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(topk_ids, num_tokens, world,
-                                                                     experts_per_rank, counts, slot, src_token);
+                                                                     experts_per_rank, 0, counts, slot, src_token);
+  return launch_status();
+}
+
+MOE_API int moe_fp8_ds_ep_plan_capacity(const int32_t* topk_ids, int32_t num_tokens, int32_t world,
+                                        int32_t experts_per_rank, int32_t capacity, int64_t* counts,
+                                        int32_t* slot, int32_t* src_token, void* stream) {
+  if (num_tokens < 0 || world < 2 || world > kMaxWorld || experts_per_rank < 1 ||
+      experts_per_rank * world != kExpertsGlobal || !counts || capacity < num_tokens || capacity < 1)
+    return MOE_ERR_INVALID_ARGUMENT;
+  if (!src_token || (num_tokens > 0 && (!topk_ids || !slot))) return MOE_ERR_INVALID_ARGUMENT;
+  ep_plan_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(topk_ids, num_tokens, world,
+                                                                     experts_per_rank, capacity, counts, slot,
+                                                                     src_token);
   return launch_status();
 }
 
@@ -200,7 +232,24 @@ MOE_API int moe_fp8_ds_ep_pack(const int32_t* topk_ids, const float* topk_weight
   if (!aligned16(hidden_states) || !aligned16(send)) return MOE_ERR_MISALIGNED;
   ep_pack_kernel<<<rows, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       topk_ids, topk_weights, static_cast<const uint8_t*>(hidden_states), hidden_states_scale, num_tokens,
-      src_token, static_cast<uint8_t*>(send));
+      src_token, 1, 1, kExpertsGlobal, static_cast<uint8_t*>(send));
+  return launch_status();
+}
+
+MOE_API int moe_fp8_ds_ep_pack_capacity(const int32_t* topk_ids, const float* topk_weights,
+                                        const void* hidden_states, const float* hidden_states_scale,
+                                        int32_t num_tokens, const int32_t* src_token, int32_t world,
+                                        int32_t experts_per_rank, int32_t capacity, void* send, void* stream) {
+  if (num_tokens < 0 || world < 2 || world > kMaxWorld || experts_per_rank * world != kExpertsGlobal ||
+      capacity < num_tokens || capacity < 1)
+    return MOE_ERR_INVALID_ARGUMENT;
+  if (!src_token || !send || (num_tokens > 0 && (!topk_ids || !topk_weights || !hidden_states ||
+                                                 !hidden_states_scale)))
+    return MOE_ERR_INVALID_ARGUMENT;
+  if ((hidden_states && !aligned16(hidden_states)) || !aligned16(send)) return MOE_ERR_MISALIGNED;
+  ep_pack_kernel<<<world * capacity, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      topk_ids, topk_weights, static_cast<const uint8_t*>(hidden_states), hidden_states_scale, num_tokens,
+      src_token, capacity, world, experts_per_rank, static_cast<uint8_t*>(send));
   return launch_status();
 }
 

@@ -8,9 +8,13 @@ batch of tokens:
 
 1. route the local tokens (fused routing kernel);
 2. dispatch: each token row goes, once, to every rank that owns at least one
-   of its 8 experts, packed with its 1x128 scales, ids and weights;
-   per-destination row counts are exchanged first so the row all-to-all
-   moves only real rows;
+   of its 8 experts, packed with its 1x128 scales, ids and weights.  With a
+   fixed ``capacity`` (the most tokens any rank brings to a step) every peer
+   gets ``capacity`` rows, real rows first and padding rows after (zero, with
+   expert ids the receiver does not own), so both all-to-alls have fixed
+   sizes and a step never waits for the device on the host.  Without one,
+   per-destination row counts are exchanged first and read on the host, so
+   the row all-to-all moves only real rows;
 3. each rank runs the layer's expert part (``moe_fp8_ds_run_routed``) on the
    rows it received, for its own experts only;
 4. combine: partial results go back to the token's home rank in fp32 (each
@@ -36,11 +40,14 @@ SCALE_BYTES = (H // 128) * 4                    # 56 fp32 scales per row
 ROW_BYTES = H + SCALE_BYTES + TOP_K * 4 + TOP_K * 4   # hidden | scales | ids | weights = 7456
 
 
-def plan_rows(ids, world, E_l):
-    """Dispatch plan: ``(counts [world] int64, slot [T, world] int64, src_token [S] int64)``.
+def plan_rows(ids, world, E_l, capacity=None):
+    """Dispatch plan: ``(counts [world] int64, slot [T, world] int64, src_token int64)``.
 
     Rows are grouped by destination rank, tokens ascending inside a group;
-    ``slot[t, r]`` is the send row of token t for rank r, or -1.
+    ``slot[t, r]`` is the send row of token t for rank r, or -1.  Compact
+    layout: ``src_token`` has ``sum(counts)`` rows.  With ``capacity``: rank
+    r's rows start at ``r * capacity`` and ``src_token`` has ``world *
+    capacity`` rows, -1 for padding.
     """
     T = ids.shape[0]
     dev = ids.device
@@ -49,21 +56,46 @@ def plan_rows(ids, world, E_l):
     dest.scatter_(1, owner, True)
     counts = dest.sum(0)
     rt = dest.t().nonzero()                                     # (rank, token) sorted by rank, token
-    src_token = rt[:, 1]
+    row = torch.arange(rt.shape[0], device=dev)
+    if capacity is None:
+        src_token = rt[:, 1]
+    else:
+        row = rt[:, 0] * capacity + row - (torch.cumsum(counts, 0) - counts)[rt[:, 0]]
+        src_token = torch.full((world * capacity,), -1, dtype=torch.long, device=dev)
+        src_token[row] = rt[:, 1]
     slot = torch.full((T, world), -1, dtype=torch.long, device=dev)
-    slot[rt[:, 1], rt[:, 0]] = torch.arange(rt.shape[0], device=dev)
+    slot[rt[:, 1], rt[:, 0]] = row
     return counts, slot, src_token
 
 
-def gather_rows(ids, w, hidden, hidden_scale, src_token):
-    """Send rows ``[S, ROW_BYTES]`` uint8 for the tokens ``src_token``."""
+def gather_rows(ids, w, hidden, hidden_scale, src_token, world=None, E_l=None, capacity=None):
+    """Send rows ``[S, ROW_BYTES]`` uint8 for the tokens ``src_token``; a -1
+    (fixed-capacity padding) gives a zero row whose 8 expert ids are the first
+    expert of the next rank, which the receiving rank ``row // capacity``
+    does not own."""
     scale_rows = hidden_scale.t()                               # [T, 56] view
-    return torch.cat([
-        hidden.view(torch.uint8).index_select(0, src_token),
-        scale_rows.index_select(0, src_token).contiguous().view(torch.uint8),
-        ids.to(torch.int32).index_select(0, src_token).contiguous().view(torch.uint8),
-        w.to(torch.float32).index_select(0, src_token).contiguous().view(torch.uint8),
-    ], dim=1)
+    pad = src_token < 0
+    S, dev = src_token.shape[0], src_token.device
+    if hidden.shape[0] == 0:     # no tokens: every row is padding
+        ids_rows = torch.zeros(S, TOP_K, dtype=torch.int32, device=dev)
+        w_rows = torch.zeros(S, TOP_K, dtype=torch.float32, device=dev)
+        hid = torch.zeros(S, H, dtype=torch.uint8, device=dev)
+        sc = torch.zeros(S, H // 128, dtype=torch.float32, device=dev)
+    else:
+        src = src_token.clamp_min(0)
+        ids_rows = ids.to(torch.int32).index_select(0, src)
+        w_rows = w.to(torch.float32).index_select(0, src)
+        hid = hidden.view(torch.uint8).index_select(0, src)
+        sc = scale_rows.index_select(0, src).contiguous()
+    if bool(pad.any()):
+        r = torch.arange(src_token.shape[0], device=src_token.device) // capacity
+        foreign = ((r + 1) % world * E_l).to(torch.int32)
+        ids_rows = torch.where(pad.unsqueeze(1), foreign.unsqueeze(1).expand_as(ids_rows), ids_rows)
+        w_rows = torch.where(pad.unsqueeze(1), torch.zeros((), dtype=w_rows.dtype, device=w_rows.device), w_rows)
+        hid = torch.where(pad.unsqueeze(1), torch.zeros((), dtype=hid.dtype, device=hid.device), hid)
+        sc = torch.where(pad.unsqueeze(1), torch.zeros((), dtype=sc.dtype, device=sc.device), sc)
+    return torch.cat([hid, sc.view(torch.uint8), ids_rows.contiguous().view(torch.uint8),
+                      w_rows.contiguous().view(torch.uint8)], dim=1)
 
 
 def pack_rows(ids, w, hidden, hidden_scale, world, E_l):
@@ -99,11 +131,11 @@ class TorchPlumbing:
     """Plan/pack/unpack/combine in PyTorch: the protocol on CPU (gloo tests)
     and the checker the library's kernels are tested against."""
 
-    def plan(self, ids, world, E_l):
-        return plan_rows(ids, world, E_l)
+    def plan(self, ids, world, E_l, capacity=None):
+        return plan_rows(ids, world, E_l, capacity)
 
-    def pack(self, ids, w, hidden, hidden_scale, src_token, rows):
-        return gather_rows(ids, w, hidden, hidden_scale, src_token[:rows].long())
+    def pack(self, ids, w, hidden, hidden_scale, src_token, rows, world=None, E_l=None, capacity=None):
+        return gather_rows(ids, w, hidden, hidden_scale, src_token[:rows].long(), world, E_l, capacity)
 
     def unpack(self, recv):
         return unpack_rows(recv)
@@ -129,24 +161,38 @@ class LibPlumbing:
     def _s(self, dev):
         return self._c.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
-    def plan(self, ids, world, E_l):
+    def plan(self, ids, world, E_l, capacity=None):
         T, dev = ids.shape[0], ids.device
         ids = ids.to(torch.int32).contiguous()
         counts = torch.empty(world, dtype=torch.int64, device=dev)
         slot = torch.empty(T, world, dtype=torch.int32, device=dev)
-        src = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
-        self._L.check(self._lib.moe_fp8_ds_ep_plan(self._p(ids), T, world, E_l, self._p(counts), self._p(slot),
-                                                   self._p(src), self._s(dev)), "moe_fp8_ds_ep_plan")
+        if capacity is None:
+            src = torch.empty(max(T * world, 1), dtype=torch.int32, device=dev)
+            st = self._lib.moe_fp8_ds_ep_plan(self._p(ids), T, world, E_l, self._p(counts), self._p(slot),
+                                              self._p(src), self._s(dev))
+        else:
+            src = torch.empty(world * capacity, dtype=torch.int32, device=dev)
+            st = self._lib.moe_fp8_ds_ep_plan_capacity(self._p(ids), T, world, E_l, capacity, self._p(counts),
+                                                       self._p(slot), self._p(src), self._s(dev))
+        self._L.check(st, "moe_fp8_ds_ep_plan")
         return counts, slot, src
 
-    def pack(self, ids, w, hidden, hidden_scale, src_token, rows):
+    def pack(self, ids, w, hidden, hidden_scale, src_token, rows, world=None, E_l=None, capacity=None):
         dev = hidden.device
         send = torch.empty(rows, ROW_BYTES, dtype=torch.uint8, device=dev)
         ids = ids.to(torch.int32).contiguous()
         w = w.to(torch.float32).contiguous()
-        self._L.check(self._lib.moe_fp8_ds_ep_pack(self._p(ids), self._p(w), self._p(hidden), self._p(hidden_scale),
-                                                   hidden.shape[0], self._p(src_token), rows, self._p(send),
-                                                   self._s(dev)), "moe_fp8_ds_ep_pack")
+        if capacity is None:
+            st = self._lib.moe_fp8_ds_ep_pack(self._p(ids), self._p(w), self._p(hidden), self._p(hidden_scale),
+                                              hidden.shape[0], self._p(src_token), rows, self._p(send),
+                                              self._s(dev))
+        else:
+            if rows != world * capacity:
+                raise ValueError("a fixed-capacity dispatch has world * capacity rows")
+            st = self._lib.moe_fp8_ds_ep_pack_capacity(self._p(ids), self._p(w), self._p(hidden),
+                                                       self._p(hidden_scale), hidden.shape[0], self._p(src_token),
+                                                       world, E_l, capacity, self._p(send), self._s(dev))
+        self._L.check(st, "moe_fp8_ds_ep_pack")
         return send
 
     def unpack(self, recv):
@@ -177,7 +223,7 @@ class ExpertParallelMoE:
     steps; ``from_library`` wires the CUDA library for all of them.
     """
 
-    def __init__(self, route_fn, expert_fn, group=None, plumbing=None):
+    def __init__(self, route_fn, expert_fn, group=None, plumbing=None, capacity=None):
         self.route_fn = route_fn
         self.expert_fn = expert_fn
         self.group = group
@@ -187,6 +233,11 @@ class ExpertParallelMoE:
         if E_GLOBAL % self.world:
             raise ValueError(f"{E_GLOBAL} experts do not split over {self.world} ranks")
         self.E_l = E_GLOBAL // self.world
+        # Fixed capacity: the same on every rank (at least the most tokens any
+        # rank brings to a step); None exchanges exact counts through the host.
+        if capacity is not None and (self.world < 2 or capacity < 1):
+            raise ValueError("a fixed capacity needs world >= 2 and capacity >= 1")
+        self.capacity = capacity
         self.last_stats = {}
         self.profile = False
         self._events = None
@@ -203,6 +254,9 @@ class ExpertParallelMoE:
         mark("start")
         ids, w = self.route_fn(routing_logits, routing_bias, routed_scaling_factor)
         mark("route")
+        if self.capacity is not None:
+            return self._forward_fixed(ids, w, hidden_states, hidden_states_scale, gemm1_weights,
+                                       gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, output, mark)
         counts, slot, src_token = pl.plan(ids, self.world, self.E_l)
         mark("plan")
         # count exchange, then the row all-to-all moves only real rows (the
@@ -226,6 +280,33 @@ class ExpertParallelMoE:
         pl.combine(back, slot, T, output)
         mark("combine")
         self.last_stats = {"sent_rows": int(send.shape[0]), "recv_rows": int(recv.shape[0])}
+        return output
+
+    def _forward_fixed(self, ids, w, hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
+                       gemm2_weights, gemm2_weights_scale, output, mark):
+        """One step with fixed per-peer capacity: no count leaves the device."""
+        T, cap, world, pl = hidden_states.shape[0], self.capacity, self.world, self.plumbing
+        if T > cap:
+            raise ValueError(f"{T} tokens exceed the fixed capacity {cap}")
+        counts, slot, src_token = pl.plan(ids, world, self.E_l, capacity=cap)
+        mark("plan")
+        send = pl.pack(ids, w, hidden_states, hidden_states_scale, src_token, world * cap,
+                       world=world, E_l=self.E_l, capacity=cap)
+        mark("pack")
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=self.group)
+        mark("row_a2a")
+        r_hidden, r_scale, r_ids, r_w = pl.unpack(recv)
+        part = self.expert_fn(r_ids, r_w, r_hidden, r_scale, gemm1_weights, gemm1_weights_scale,
+                              gemm2_weights, gemm2_weights_scale, self.rank * self.E_l)
+        mark("experts")
+        back = torch.empty_like(part)
+        dist.all_to_all_single(back, part, group=self.group)
+        mark("partial_a2a")
+        pl.combine(back, slot, T, output)
+        mark("combine")
+        # real row counts only on request: reading them would synchronise
+        self.last_stats = {"sent_rows": int(counts.sum())} if self.profile else {}
         return output
 
     def _marker(self, device):
@@ -252,8 +333,9 @@ class ExpertParallelMoE:
     __call__ = forward
 
 
-def from_library(group=None):
-    """ExpertParallelMoE whose routing, plumbing and expert compute run in libmoe_fp8_ds.so."""
+def from_library(group=None, capacity=None):
+    """ExpertParallelMoE whose routing, plumbing and expert compute run in libmoe_fp8_ds.so
+    (``capacity``: fixed per-peer rows, see ``ExpertParallelMoE``)."""
     import ctypes
     import importlib
     from . import _lib
@@ -280,4 +362,4 @@ def from_library(group=None):
             K.run_with_workspace(args, ws, routed=True)
         return out
 
-    return ExpertParallelMoE(route_fn, expert_fn, group, plumbing=LibPlumbing())
+    return ExpertParallelMoE(route_fn, expert_fn, group, plumbing=LibPlumbing(), capacity=capacity)

@@ -223,6 +223,23 @@ MOE_API int moe_fp8_ds_ep_pack(const int32_t* topk_ids, const float* topk_weight
                                const float* hidden_states_scale, int32_t num_tokens, const int32_t* src_token,
                                int32_t rows, void* send, void* stream);
 
+/* Fixed-capacity form of the two calls above (world >= 2, capacity >= T):
+ * rank r's send rows are [r*capacity, (r+1)*capacity), its real rows first
+ * (token order), then padding rows (src_token = -1).  Every peer then gets
+ * exactly `capacity` rows, so the all-to-alls need no counts on the host and
+ * a step runs without a device-to-host synchronisation.  A padding row is
+ * zero except its 8 expert ids, all equal to the first expert of rank r+1
+ * (mod world): valid, but not owned by the receiver, whose layer gives the
+ * row no work and a zero partial.  slot[t][r] points into this layout;
+ * send holds world*capacity rows.                                            */
+MOE_API int moe_fp8_ds_ep_plan_capacity(const int32_t* topk_ids, int32_t num_tokens, int32_t world,
+                                        int32_t experts_per_rank, int32_t capacity, int64_t* counts,
+                                        int32_t* slot, int32_t* src_token, void* stream);
+MOE_API int moe_fp8_ds_ep_pack_capacity(const int32_t* topk_ids, const float* topk_weights,
+                                        const void* hidden_states, const float* hidden_states_scale,
+                                        int32_t num_tokens, const int32_t* src_token, int32_t world,
+                                        int32_t experts_per_rank, int32_t capacity, void* send, void* stream);
+
 /* Split received rows into the layer's argument layout: hidden e4m3
  * [rows, 7168], scales fp32 [56, rows], ids int32 [rows, 8], weights fp32
  * [rows, 8] (the inputs of moe_fp8_ds_run_routed).                          */

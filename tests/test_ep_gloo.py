@@ -44,7 +44,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, T, q):
+def _worker(rank, world, port, T, q, capacity=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world,
                             timeout=datetime.timedelta(seconds=60))
@@ -62,7 +62,8 @@ def _worker(rank, world, port, T, q):
         def expert_fn(ids, w, hidden, scale, w13, s13, w2, s2, offset):
             return standin_experts(ids, w, hidden, scale, w13, s13, w2, s2, offset, E_l)
 
-        layer = ep_mod.ExpertParallelMoE(route_fn, expert_fn)
+        layer = ep_mod.ExpertParallelMoE(route_fn, expert_fn, capacity=capacity)
+        layer.profile = True    # row statistics (CPU: no events)
         logits, bias, hs, hss = pkg.inputs.make_token_inputs(T, seed=100 + rank)
         dummy = torch.empty(E_l, 1)
         out = torch.empty(T, H, dtype=torch.bfloat16)
@@ -81,12 +82,14 @@ def _worker(rank, world, port, T, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
-def test_ep_protocol_matches_single_process(world):
+@pytest.mark.parametrize("world,capacity", [(2, None), (4, None), (8, None), (2, 32), (8, 24)])
+def test_ep_protocol_matches_single_process(world, capacity):
+    """Exact counts through the host (capacity None), or fixed per-peer capacity
+    with padding rows (capacity >= the 24 tokens each rank brings)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 24, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 24, q, capacity)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]

@@ -29,7 +29,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, T, q):
+def _worker(rank, world, port, T, q, capacity=None):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
@@ -45,7 +45,7 @@ def _worker(rank, world, port, T, q):
         ref = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
         pkg.kernel(logits, bias, hs, hss, w13, s13, w2, s2, 0, 2.5, ref)
         sl = slice(rank * E_l, (rank + 1) * E_l)
-        layer = ep.from_library()
+        layer = ep.from_library(capacity=capacity)
         out = torch.full((T, 7168), float("nan"), dtype=torch.bfloat16, device=dev)
         layer(logits, bias, hs, hss, w13[sl], s13[sl], w2[sl], s2[sl], 2.5, out)
         out2 = torch.empty_like(out)
@@ -74,14 +74,16 @@ def _worker(rank, world, port, T, q):
         dist.destroy_process_group()
 
 
-def test_expert_parallel_two_gpus(cuda_dev):
+@pytest.mark.parametrize("capacity", [None, 64])
+def test_expert_parallel_two_gpus(cuda_dev, capacity):
+    """Exact counts through the host, or fixed per-peer capacity (64 >= 48 tokens)."""
     world = 2
     if torch.cuda.device_count() < world:
         pytest.skip("needs two GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, 48, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, 48, q, capacity)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=300) for _ in range(world)]
