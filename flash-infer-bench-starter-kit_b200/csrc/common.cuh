@@ -84,6 +84,18 @@ __device__ __forceinline__ int ld_acquire_gpu(const int* p) {
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
+// Counter updates that publish (release) and read (acquire) the data a CTA
+// wrote before them.  Used after a CTA-wide barrier by one thread: the barrier
+// orders the other threads' stores before the release (cumulativity), so one
+// signalling thread replaces a fence in every thread.
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void red_add_release_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 // Order this thread's earlier (generic-proxy) observations before its later
 // async-proxy (TMA) accesses.
 // Work unit u of a grouped GEMM -> (token tile mt, weight tile nt), token-tile

@@ -367,17 +367,15 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
 #pragma unroll
           for (int jj = 0; jj < C::CPW; ++jj)
             __stcg(mine + ((size_t)w * BN + j0 + jj) * 128 + f, acc[w][jj]);
-        __threadfence();
         named_bar_sync(1, C::NEPI);
         const int c_lo = sch.first_cta(r, C::KSTEPS);
         const int c_hi = sch.last_cta(r, C::KSTEPS);
         if (et == 0) {
-          const int old = atomicAdd(p.counters + u, 1);
+          const int old = atom_add_acq_rel_gpu(p.counters + u, 1);   // publishes this share, acquires the others
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
         }
         named_bar_sync(1, C::NEPI);
         if (!last_flag[0]) continue;
-        __threadfence();
         if (c_hi - c_lo == 1) {
           // Two contributors: fp32 addition is commutative, so adding the other
           // CTA's partial to our registers is the same sum whoever is last.
@@ -445,9 +443,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
         }
         if (p.early_start) {
           // all warpgroups' stores of this unit, then one release increment
-          __threadfence();
           named_bar_sync(1, C::NEPI);
-          if (et == 0) atomicAdd(p.ready + tile.x, 1);
+          if (et == 0) red_add_release_gpu(p.ready + tile.x, 1);
         } else {
           named_bar_sync(2 + wg, 128);
         }

@@ -347,17 +347,15 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
           for (int w = 0; w < C::COLS / 4; ++w)
             __stcg(reinterpret_cast<float4*>(mine + h * 128) + w,
                    make_float4(acc[h][4 * w], acc[h][4 * w + 1], acc[h][4 * w + 2], acc[h][4 * w + 3]));
-        __threadfence();
         named_bar_sync(1, C::NEPI);
         const int c_lo = sch.first_cta(r, C::KSTEPS);
         const int c_hi = sch.last_cta(r, C::KSTEPS);
         if (et == 0) {
-          const int old = atomicAdd(p.counters + u, 1);
+          const int old = atom_add_acq_rel_gpu(p.counters + u, 1);   // publishes this share, acquires the others
           last_flag[0] = (old == c_hi - c_lo) ? 1 : 0;
         }
         named_bar_sync(1, C::NEPI);
         if (!last_flag[0]) continue;
-        __threadfence();
 #pragma unroll
         for (int h = 0; h < C::NH; ++h)
 #pragma unroll
