@@ -178,6 +178,18 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
 // 3D view of a K-major e4m3 matrix [rows, K]: x = byte inside a 128-wide K
 // block, y = row, z = K block; a box covers box_rows rows x kblocks K blocks,
 // landing as kblocks consecutive 128-byte-swizzled [box_rows x 128] tiles.
+// 2D view of a K-major e4m3 matrix [rows, K] with a 128-byte x 1-row box, for
+// tile::gather4 row gathers.
+bool encode_rows_2d(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows) {
+  cuuint64_t dims[2] = {K, rows};
+  cuuint64_t strides[1] = {K};
+  cuuint32_t box[2] = {128, 1};
+  cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool encode_kmajor(CUtensorMap* m, const void* base, uint64_t K, uint64_t rows, uint32_t box_rows,
                    uint32_t kblocks) {
   cuuint64_t dims[3] = {128, rows, K / 128};
@@ -312,8 +324,12 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
       return MOE_ERR_INVALID_ARGUMENT;
   } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
+  // After the fused front kernel GEMM1 gathers token rows itself: a map of
+  // hidden_states with 128-byte x 1-row boxes (tile::gather4).
+  const bool gather1 = !routed && T <= kFrontMaxTokens;
   if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
-      !encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1, ks1) ||
+      !(gather1 ? encode_rows_2d(&tm_b1, a->hidden_states, kHidden, (uint64_t)T)
+                : encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1, ks1)) ||
       !encode_kmajor(&tm_w2, a->gemm2_weights, kInter, (uint64_t)E_l * kHidden, 128, ks2) ||
       !encode_kmajor(&tm_b2, inter, kInter, 2ull * P.R_cap, (uint32_t)(2 * P.bn2), ks2))
     return MOE_ERR_INVALID_ARGUMENT;
@@ -357,6 +373,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
   g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
+  g1.row_token = row_token;
   g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
   ce = P.tm     ? launch_gemm_tm(1, &tm_w1, &tm_b1, &tm_bs1, &tm_ws1, g1, P.grid1, s)
                 : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);

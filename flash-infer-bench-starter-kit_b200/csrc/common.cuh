@@ -207,6 +207,19 @@ __device__ __forceinline__ void tma_load_3d(const CUtensorMap* map, uint64_t* ba
       : "memory");
 }
 
+// Row gather (tile::gather4) of a 2D K-major e4m3 matrix whose tensor map
+// box is 128 bytes x 1 row: rows r0..r3, bytes x..x+127 (x a multiple of
+// 128), landing as four consecutive 128-byte-swizzled rows at smem_dst.
+__device__ __forceinline__ void tma_gather4(const CUtensorMap* map, uint64_t* bar, void* smem_dst, int32_t x,
+                                            int32_t r0, int32_t r1, int32_t r2, int32_t r3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
+      "l"(policy)
+      : "memory");
+}
+
 // 2D tiled load: x = innermost element index (its byte offset must be a
 // multiple of 16), y = row.
 __device__ __forceinline__ void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* smem_dst,

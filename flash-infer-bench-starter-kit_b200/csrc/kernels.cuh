@@ -21,6 +21,10 @@ struct GemmParams {
   // the second reaches front_ctas (no grid-dependency wait).  nullptr: off.
   int* front_sync;
   int front_ctas;
+  // GEMM1 after the fused front kernel: token rows are gathered straight from
+  // hidden_states (tm_b is a 128-byte x 1-row map of it, tile::gather4) by
+  // the permuted-row -> token map, so the activation is never materialised.
+  const int32_t* row_token;
   int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048] (row pairs, or hi/lo planes)

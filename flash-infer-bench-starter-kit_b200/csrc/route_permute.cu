@@ -416,13 +416,14 @@ scatter_kernel(const int32_t* __restrict__ topk_ids, const uint8_t* __restrict__
 
 // --------------------------------------------------------------------------
 // Fused front end for small batches (T <= kFrontMaxTokens): routing, row
-// assignment and activation gather in ONE launch instead of three.
+// assignment and the activation scales in ONE launch instead of three (the
+// token rows are gathered by GEMM1 itself, tile::gather4 from hidden_states).
 //
 // CTA g routes tokens 8g..8g+7 (one warp each) and publishes its byte masks;
 // after a grid-wide barrier every CTA recomputes the per-expert row offsets
 // from all masks (at most 32 x E_l bytes, cheaper than another launch), then
-// assigns rows to its own tokens and copies their hidden rows and scales into
-// the permuted activation.  CTA 0 also writes the segment offsets, the GEMM
+// assigns rows to its own tokens (inverse map, row -> token map) and copies
+// their 1x128 scales into the permuted scale array.  CTA 0 also writes the segment offsets, the GEMM
 // tile lists and zeroes the stream-K counters.  All CTAs are resident (at
 // most 32 small CTAs); the barrier wait is bounded and raises the device error
 // word instead of hanging.
@@ -570,7 +571,7 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
       atomicExch(front_sync, 1);
     }
   }
-  // ---- phase 3: rows of own tokens, inverse map, activation gather
+  // ---- phase 3: rows of own tokens, inverse map, row -> token map, scales
   if (threadIdx.x < kRouteTokens * kTopK) {
     const int w8 = threadIdx.x / kTopK, k = threadIdx.x % kTopK;
     const int tt = blockIdx.x * kRouteTokens + w8;
@@ -586,36 +587,15 @@ front_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__
     }
   }
   __syncthreads();
-  // copy with all of a thread's loads in flight before its stores
-  constexpr int kVec = kHidden / 16;
-  constexpr int kBatch = 8;
-  const int nvec = s_n * kVec;
-  for (int v0 = 0; v0 < nvec; v0 += kBatch * blockDim.x) {
-    uint4 buf[kBatch];
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int v = v0 + u * blockDim.x + threadIdx.x;
-      if (v < nvec) {
-        const int2 rt = s_list[v / kVec];
-        buf[u] = __ldg(reinterpret_cast<const uint4*>(hidden + (size_t)rt.y * kHidden) + v % kVec);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-      const int v = v0 + u * blockDim.x + threadIdx.x;
-      if (v < nvec) {
-        const int2 rt = s_list[v / kVec];
-        reinterpret_cast<uint4*>(act + (size_t)rt.x * kHidden)[v % kVec] = buf[u];
-      }
-    }
-  }
+  // The token rows themselves are not copied: GEMM1 gathers them from
+  // hidden_states by row_token (tile::gather4).  Their 1x128 scales are.
   for (int v = threadIdx.x; v < s_n * kHiddenBlocks; v += blockDim.x) {
     const int2 rt = s_list[v / kHiddenBlocks];
     const int kb = v % kHiddenBlocks;
     act_scale[(size_t)kb * R_cap + rt.x] = __ldg(hs_scale + (size_t)kb * T + rt.y);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {     // this CTA's rows of act / act_scale are written
+  if (threadIdx.x == 0) {     // this CTA's rows of row_token / act_scale are written
     __threadfence();
     atomicAdd(front_sync + 1, 1);
   }
