@@ -324,8 +324,11 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
       return MOE_ERR_INVALID_ARGUMENT;
   } else {
   const uint32_t ks1 = (uint32_t)gemm_k_per_stage(1, P.bn1), ks2 = (uint32_t)gemm_k_per_stage(2, P.bn2);
-  // After the fused front kernel GEMM1 gathers token rows itself: a map of
-  // hidden_states with 128-byte x 1-row boxes (tile::gather4).
+  // After the fused front kernel (T <= 256, 16-token tiles) GEMM1 gathers token
+  // rows itself: a map of hidden_states with 128-byte x 1-row boxes
+  // (tile::gather4), rows by row_token.  With wider tiles (larger T) the four
+  // rows per copy cost more than the scatter kernel's copy: measured T=1024
+  // 422 vs 387 us, so there the permuted activation is materialised.
   const bool gather1 = !routed && T <= kFrontMaxTokens;
   if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
       !(gather1 ? encode_rows_2d(&tm_b1, a->hidden_states, kHidden, (uint64_t)T)
@@ -360,8 +363,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
     if (ce != cudaSuccess) return cuda_fail(ce);
     mark_stage(2, s);
     ce = launch_scatter(ids, masks8, P.NB8, bases, T, E_l, a->local_expert_offset, P.R_cap,
-                        a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale,
-                        s);
+                        a->hidden_states, a->hidden_states_scale, inv, row_token, act, act_scale, s);
     if (ce != cudaSuccess) return cuda_fail(ce);
   }
 
@@ -373,7 +375,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);
   g1.front_sync = front ? reinterpret_cast<int*>(at(P.front_sync)) : nullptr;
-  g1.row_token = row_token;
+  g1.row_token = front ? row_token : nullptr;   // GEMM1 gathers token rows by row_token
   g1.front_ctas = (T + kRouteTokens - 1) / kRouteTokens;
   ce = P.tm     ? launch_gemm_tm(1, &tm_w1, &tm_b1, &tm_bs1, &tm_ws1, g1, P.grid1, s)
                 : launch_gemm(1, P.bn1, &tm_w1, &tm_b1, g1, P.grid1, s);

@@ -9,8 +9,11 @@
 // fills the tensor core's M dimension and the weight stream is the only large
 // operand.  Both operands are K-major e4m3 tiles loaded by TMA with 128-byte
 // swizzling; one tcgen05.mma of K=32 is issued four times per 128-wide K block.
-// The token operand of GEMM1 is the permuted activation the scatter kernel
-// gathered, so each token tile is one TMA box.
+// After the fused front kernel (small batches) the token operand of GEMM1 is
+// gathered by the producer straight from hidden_states (tile::gather4, four
+// 128-byte rows per copy, rows by the permuted-row -> token map); for larger
+// batches it is the permuted activation the scatter kernel wrote, one TMA box
+// per token tile, as is GEMM2's token operand (the intermediate).
 //
 // Block scales: the fp32 128x128 weight scale is a scalar per (tile, K block),
 // the fp32 1x128 activation scale is per token column.  Because they are
@@ -177,7 +180,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           fence_proxy_async();
           gathered = true;
         }
-        if (KIND == 1 && early1) {
+        if (KIND == 1 && p.row_token != nullptr) {
           // token rows straight from hidden_states: four rows per gather, rows
           // past the tile repeat its first token (their columns are not used)
           if (mt != tok_mt) {

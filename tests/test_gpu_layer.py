@@ -24,8 +24,7 @@ from conftest import cached_inputs, load_golden
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 1e-2, 2e-2
-TM_MIN_TOKENS = 1536
-FRONT_MAX_TOKENS = 256     # fused front kernel (routing + row map + scales), GEMM1 gathers token rows         # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
+TM_MIN_TOKENS = 1536         # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
 
 
 def _mods():
@@ -209,7 +208,7 @@ def check_stages(pkg, oracle, inp, inp_dev, bn, path, experts=None):
     off = inp["local_expert_offset"]
     out, ws, lay = run_layer(pkg, inp_dev, bn=bn, path=path)
     tm = path == 2 or (path == 0 and T >= TM_MIN_TOKENS)
-    front = not tm and T <= FRONT_MAX_TOKENS
+    front = not tm and T <= 256    # fused front kernel: GEMM1 gathers token rows itself (no act)
     R = lay.row_capacity
     # routing
     ids_ref, w_ref, _ = oracle.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"],
@@ -230,7 +229,7 @@ def check_stages(pkg, oracle, inp, inp_dev, bn, path, experts=None):
     A = oracle.dequant_hidden(inp["hidden_states"], inp["hidden_states_scale"])
     down = ws_view(ws, lay.down, R * 7168, torch.float32).view(R, 7168)[:nrows].cpu()
     # permuted e4m3 rows + scales
-    if not front:   # after the fused front kernel GEMM1 gathers token rows itself
+    if not front:
         act = ws_view(ws, lay.act, R * 7168, torch.uint8).view(R, 7168)[:nrows].cpu()
         assert torch.equal(act, inp["hidden_states"].view(torch.uint8)[row_tok])
     act_sc = ws_view(ws, lay.act_scale, 56 * R, torch.float32).view(56, R)[:, :nrows].cpu()
