@@ -71,6 +71,27 @@ int device_info(DeviceInfo* out) {
   return d.major == 10 ? MOE_OK : MOE_ERR_NO_DEVICE;
 }
 
+}  // namespace
+
+void* current_cu_context() {
+  using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+  static std::atomic<CtxGetCurrentFn> fn_cache{nullptr};
+  CtxGetCurrentFn fn = fn_cache.load(std::memory_order_acquire);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !p)
+      return nullptr;
+    fn = reinterpret_cast<CtxGetCurrentFn>(p);
+    fn_cache.store(fn, std::memory_order_release);
+  }
+  CUcontext ctx = nullptr;
+  return fn(&ctx) == CUDA_SUCCESS ? static_cast<void*>(ctx) : nullptr;
+}
+
+namespace {
+
 // Token-tile width per GEMM from the expected tokens per active expert.
 int pick_bn(int T, int E_l) {
   const double per_expert = (double)T * kTopK / kExpertsGlobal;

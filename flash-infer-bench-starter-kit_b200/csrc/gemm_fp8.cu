@@ -509,7 +509,10 @@ static cudaError_t launch_one(const CUtensorMap* tm_w, const CUtensorMap* tm_b, 
   using P = Pick<KIND, BN>;
   using C = CfgOf<KIND, BN>;
   auto kern = moe_gemm_kernel<KIND, BN, P::S, P::W, P::K, P::O>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  static std::atomic<void*> seen[kMaxCachedDevices];
+  cudaError_t e = once_per_context(seen, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  });
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, p);
 }

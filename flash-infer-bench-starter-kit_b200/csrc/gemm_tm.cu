@@ -467,7 +467,10 @@ static cudaError_t launch_tm_one(const CUtensorMap* tm_w, const CUtensorMap* tm_
   using P = TmPick<KIND>;
   using C = TmCfgOf<KIND>;
   auto kern = moe_gemm_tm_kernel<KIND, P::KS, P::S>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  static std::atomic<void*> seen[kMaxCachedDevices];
+  cudaError_t e = once_per_context(seen, [&] {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  });
   if (e != cudaSuccess) return e;
   return launch_pdl(kern, dim3(grid), dim3(C::THREADS), C::SMEM, st, *tm_w, *tm_b, *tm_bs, *tm_ws, p);
 }

@@ -3,6 +3,8 @@
 
 #include "common.cuh"
 
+#include <atomic>
+
 namespace moe {
 
 // Work description read by the grouped GEMMs (written by scan_kernel).
@@ -92,6 +94,24 @@ __host__ __device__ __forceinline__ WorkSched make_work_sched_for(int n_mt, int 
 
 __device__ __forceinline__ WorkSched make_work_sched(int n_mt, int NT, int ITERS) {
   return make_work_sched_for(n_mt, NT, ITERS, (int)gridDim.x, (int)blockIdx.x);
+}
+
+// Per-kernel launch set-up (the dynamic shared memory opt-in, checks of the
+// compiled kernel) done once per device and CUDA context instead of on every
+// launch: `seen` is the kernel's own table, indexed by device.
+constexpr int kMaxCachedDevices = 64;
+void* current_cu_context();   // the calling thread's CUcontext, nullptr if none
+template <typename SetUp>
+cudaError_t once_per_context(std::atomic<void*>* seen, SetUp set_up) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  void* ctx = current_cu_context();
+  if (dev < 0 || dev >= kMaxCachedDevices || ctx == nullptr) return set_up();
+  if (seen[dev].load(std::memory_order_acquire) == ctx) return cudaSuccess;
+  e = set_up();
+  if (e == cudaSuccess) seen[dev].store(ctx, std::memory_order_release);
+  return e;
 }
 
 size_t gemm_partials_bytes(int kind, int bn, int grid);

@@ -66,9 +66,10 @@ def _device_index(device: torch.device | None) -> int:
     return device.index
 
 
-def _entry(device: torch.device, nbytes: int) -> _Workspace:
+def _entry(device: torch.device, nbytes: int, stream: torch.cuda.Stream | None = None) -> _Workspace:
     idx = _device_index(device)
-    stream = torch.cuda.current_stream(idx)
+    if stream is None:
+        stream = torch.cuda.current_stream(idx)
     key = (idx, stream.cuda_stream)
     with _ws_lock:
         ent = _workspaces.get(key)
@@ -109,13 +110,14 @@ def release_workspaces(device: torch.device | None = None, stream: torch.cuda.St
 
 
 def _check_tensor(name, t, dtype, shape, device):
+    # (cheap comparisons first: this runs for every argument of every call)
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor")
-    if t.device != device:
+    if t.get_device() != device.index:
         raise ValueError(f"{name} is on {t.device}, expected {device}")
-    if t.dtype != dtype:
+    if t.dtype is not dtype:
         raise TypeError(f"{name} has dtype {t.dtype}, expected {dtype}")
-    if tuple(t.shape) != tuple(shape):
+    if t.shape != shape:
         raise ValueError(f"{name} has shape {tuple(t.shape)}, expected {tuple(shape)}")
     if not t.is_contiguous():
         raise ValueError(f"{name} must be contiguous")
@@ -193,15 +195,21 @@ def kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
     args = build_args(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
                       local_expert_offset, routed_scaling_factor, output)
-    with torch.cuda.device(hidden_states.device):
-        ent = _entry(hidden_states.device, workspace_bytes(args.num_tokens, args.num_local_experts))
-        run_with_workspace(args, ent.buf)
-        # Under CUDA-graph capture the launches become graph nodes and the
-        # last-use event is not recorded (an event recorded in a capture cannot
-        # be waited on outside it); synchronise the replay stream before
-        # read_device_error after replays.
-        if not torch.cuda.is_current_stream_capturing():
-            ent.event.record()
+    dev = hidden_states.device
+    if torch.cuda.current_device() != dev.index:
+        with torch.cuda.device(dev):
+            return kernel(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                          gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                          local_expert_offset, routed_scaling_factor, output)
+    stream = torch.cuda.current_stream(dev.index)
+    ent = _entry(dev, workspace_bytes(args.num_tokens, args.num_local_experts), stream)
+    run_with_workspace(args, ent.buf, stream.cuda_stream)
+    # Under CUDA-graph capture the launches become graph nodes and the
+    # last-use event is not recorded (an event recorded in a capture cannot
+    # be waited on outside it); synchronise the replay stream before
+    # read_device_error after replays.
+    if not torch.cuda.is_current_stream_capturing():
+        ent.event.record(stream)
 
 
 def read_device_error(device: torch.device | None = None) -> int:
