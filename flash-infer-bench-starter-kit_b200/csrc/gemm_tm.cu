@@ -323,9 +323,14 @@ moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_consta
           for (int e = 0; e < 2; ++e) {
             const int h = (cc + e) >> 2, c0 = ((cc + e) & 3) * 16;
             const float cf = h ? cB[kk] : cA[kk];
+            const float2 cf2 = make_float2(cf, cf);
 #pragma unroll
-            for (int x = 0; x < 16; ++x)
-              acc[h][c0 + x] = fmaf(pv[e][x], cf, acc[h][c0 + x]);
+            for (int x = 0; x < 16; x += 2) {   // paired FMAs (one fma.rn.f32x2 per two columns)
+              const float2 r = __ffma2_rn(make_float2(pv[e][x], pv[e][x + 1]), cf2,
+                                          make_float2(acc[h][c0 + x], acc[h][c0 + x + 1]));
+              acc[h][c0 + x] = r.x;
+              acc[h][c0 + x + 1] = r.y;
+            }
           }
         }
       }
