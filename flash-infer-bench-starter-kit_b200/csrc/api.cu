@@ -350,7 +350,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   // (tile::gather4), rows by row_token.  With wider tiles (larger T) the four
   // rows per copy cost more than the scatter kernel's copy: measured T=1024
   // 422 vs 387 us, so there the permuted activation is materialised.
-  const bool gather1 = !routed && T <= kFrontMaxTokens;
+  const bool gather1 = !routed && T <= kFrontMaxTokens && P.bn1 <= kGatherMaxBN;
   if (!encode_kmajor(&tm_w1, a->gemm1_weights, kHidden, (uint64_t)E_l * kGemm1Out, 128, ks1) ||
       !(gather1 ? encode_rows_2d(&tm_b1, a->hidden_states, kHidden, (uint64_t)T)
                 : encode_kmajor(&tm_b1, act, kHidden, (uint64_t)P.R_cap, (uint32_t)P.bn1, ks1)) ||
@@ -360,7 +360,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   }
 
   cudaError_t ce;
-  const bool front = !routed && T <= kFrontMaxTokens && !P.tm;
+  const bool front = !routed && T <= kFrontMaxTokens && !P.tm && P.bn1 <= kGatherMaxBN;
   if (front) {
     // Small batch: routing, row assignment and gather in one launch.
     mark_stage(0, s);
@@ -391,7 +391,7 @@ int run_impl(const moe_fp8_ds_args* a, void* ws, uint64_t ws_bytes, void* stream
   GemmParams g1{};
   g1.tiles = tiles1; g1.sched = sched; g1.w_scale = a->gemm1_weights_scale;
   g1.b_scale = act_scale;
-  g1.counters = cnt1; g1.ready = ready; g1.seg = seg; g1.bn_prev = 0;
+  g1.counters = cnt1; g1.ready = ready; g1.bn_prev = 0;
   g1.early_start = front ? 1 : 0; g1.partials = reinterpret_cast<float*>(at(P.partials1));
   g1.inter = inter; g1.inter_scale = inter_scale; g1.down = nullptr; g1.err = err; g1.R_cap = P.R_cap;
   mark_stage(3, s);

@@ -70,7 +70,7 @@ struct GemmCfg {
   static constexpr int CPW = BN / NWG;                      // token columns per warpgroup
   static constexpr int SLOT = KS * NW * BN;                 // promotion coefficients per iteration
   static constexpr int RING = 3;                            // slots (prefetch distance 2)
-  static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4 + BN * 4;
+  static constexpr int AUX = 2048 + RING * SLOT * 4 + NWG * 4 * CPW * 4 + (BN <= kGatherMaxBN ? BN * 4 : 0);
   static constexpr int SMEM = 1024 + STAGES * STAGE + AUX;
   static_assert(KB % KS == 0, "K steps");
   static_assert(TMEM_USED <= 512 && NBUF >= 2, "TMEM budget");
@@ -152,7 +152,7 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
       int issued = 0;
       int ready_e = -1;                 // GEMM2: expert whose intermediate is known complete
       bool gathered = !early1;          // GEMM1 after the front kernel: row map and scales written
-      int tok_mt = -1;                  // token tile whose rows s_tok holds
+      [[maybe_unused]] int tok_mt = -1;   // token tile whose rows s_tok holds
       bool ok = true;
       for (int i = 0; i < n_iter; ++i) {
         int u, ks, r;
@@ -180,7 +180,8 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
           fence_proxy_async();
           gathered = true;
         }
-        if (KIND == 1 && p.row_token != nullptr) {
+        if constexpr (KIND == 1 && BN <= kGatherMaxBN) {
+          if (p.row_token != nullptr) {
           // token rows straight from hidden_states: four rows per gather, rows
           // past the tile repeat its first token (their columns are not used)
           if (mt != tok_mt) {
@@ -192,6 +193,9 @@ moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant_
             for (int g4 = 0; g4 < BN / 4; ++g4)
               tma_gather4(&tm_b, &full[s], bdst + kk * C::B_TILE + g4 * 512, (z + kk) * 128, s_tok[4 * g4],
                           s_tok[4 * g4 + 1], s_tok[4 * g4 + 2], s_tok[4 * g4 + 3], pol_b);
+          } else {
+            tma_load_3d(&tm_b, &full[s], st + C::NW * KS * C::W_TILE, 0, tile.y, z, pol_b);
+          }
         } else {
           tma_load_3d(&tm_b, &full[s], st + C::NW * KS * C::W_TILE, 0, KIND == 1 ? tile.y : 2 * tile.y, z, pol_b);
         }

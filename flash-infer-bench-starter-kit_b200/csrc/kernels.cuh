@@ -8,6 +8,10 @@
 namespace moe {
 
 // Work description read by the grouped GEMMs (written by scan_kernel).
+// Widest GEMM1 token tile that gathers its rows with tile::gather4 (after the
+// fused front kernel); wider tiles load the permuted activation.
+constexpr int kGatherMaxBN = 32;
+
 struct GemmParams {
   const int4* tiles;          // (local expert, first row, rows, 0) per token tile
   const int32_t* sched;       // sched[0] = #tiles for GEMM1, sched[1] = #tiles for GEMM2
@@ -15,7 +19,16 @@ struct GemmParams {
   const float* b_scale;       // GEMM1: act_scale [56, R_cap]; GEMM2: inter_scale [16, R_cap]
   int32_t* counters;          // stream-K arrival counters, one per output tile
   int* ready;                 // per local expert: GEMM1 units finished (GEMM1 adds, GEMM2 waits)
-  const int32_t* seg;         // per-expert row offsets (GEMM2: rows of expert e)
+  union {
+    const int32_t* seg;         // GEMM2: per-expert row offsets (rows of expert e)
+    // GEMM1 after the fused front kernel: token rows are gathered straight
+    // from hidden_states (tm_b is a 128-byte x 1-row map of it, tile::gather4)
+    // by this permuted-row -> token map, so the activation is never
+    // materialised (compiled into the GEMM1 variants with token tiles of at
+    // most kGatherMaxBN rows; the host uses the fused front kernel only for
+    // those).  Shares its slot with seg, which GEMM1 does not read.
+    const int32_t* row_token;
+  };
   int bn_prev;                // GEMM2: GEMM1's token-tile width
   // e4m3 GEMM1 after the fused front kernel: front_sync[0] = 1 once the tile
   // lists are written, front_sync[1] counts front CTAs whose gather is done.
@@ -23,10 +36,6 @@ struct GemmParams {
   // the second reaches front_ctas (no grid-dependency wait).  nullptr: off.
   int* front_sync;
   int front_ctas;
-  // GEMM1 after the fused front kernel: token rows are gathered straight from
-  // hidden_states (tm_b is a 128-byte x 1-row map of it, tile::gather4) by
-  // the permuted-row -> token map, so the activation is never materialised.
-  const int32_t* row_token;
   int early_start;            // GEMM2: start before GEMM1 completes (small batches)
   float* partials;            // stream-K partial tiles, [grid][2][NW][BN][128]
   uint8_t* inter;             // GEMM1 output: e4m3 [2*R_cap, 2048] (row pairs, or hi/lo planes)
