@@ -74,6 +74,12 @@ def test_argument_validation_without_gpu(pkg):
     assert lib.moe_fp8_ds_ep_plan(None, 4, 2, 128, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_ep_pack(None, None, None, None, 4, None, 0, None, None) == L.MOE_OK
     assert lib.moe_fp8_ds_ep_pack(None, None, None, None, 4, None, 2, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    # fixed capacity: world >= 2, capacity >= tokens, src_token and counts required
+    assert lib.moe_fp8_ds_ep_plan_capacity(None, 0, 1, 256, 4, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_plan_capacity(None, 8, 2, 128, 4, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_plan_capacity(None, 0, 2, 128, 4, cnt, None, None, None) == L.MOE_ERR_INVALID_ARGUMENT
+    assert lib.moe_fp8_ds_ep_pack_capacity(None, None, None, None, 8, None, 2, 128, 4, None, None) == \
+        L.MOE_ERR_INVALID_ARGUMENT
     assert lib.moe_fp8_ds_ep_unpack(None, 0, None, None, None, None, None) == L.MOE_OK
     assert lib.moe_fp8_ds_ep_combine(None, None, 0, 2, None, None) == L.MOE_OK
     assert lib.moe_fp8_ds_ep_combine(None, None, 4, 9, None, None) == L.MOE_ERR_INVALID_ARGUMENT
