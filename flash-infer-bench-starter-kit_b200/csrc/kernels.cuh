@@ -7,11 +7,14 @@
 
 namespace moe {
 
-// Work description read by the grouped GEMMs (written by scan_kernel).
 // Widest GEMM1 token tile that gathers its rows with tile::gather4 (after the
 // fused front kernel); wider tiles load the permuted activation.
 constexpr int kGatherMaxBN = 32;
 
+// Work description read by the grouped GEMMs (written by scan_kernel).  Its
+// size matters: every field is a kernel parameter, and a larger block made
+// the 64-token GEMM1 spill registers, so a field one GEMM never reads may
+// share a slot with the other GEMM's (seg / row_token).
 struct GemmParams {
   const int4* tiles;          // (local expert, first row, rows, 0) per token tile
   const int32_t* sched;       // sched[0] = #tiles for GEMM1, sched[1] = #tiles for GEMM2
