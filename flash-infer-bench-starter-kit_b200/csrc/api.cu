@@ -31,7 +31,7 @@ EncodeTiledFn g_encode = nullptr;
 int g_bn_override[2] = {0, 0};
 int g_path_override = 0;          // 0 automatic, 1 weights-on-M e4m3 GEMMs, 2 tokens-on-M e4m3 GEMMs
 // From this batch size the layer runs the tokens-on-M e4m3 GEMMs (gemm_tm.cu).
-constexpr int kTmMinTokens = 1536;
+constexpr int kTmMinTokens = 1280;
 cudaEvent_t g_stage_events[7] = {};
 bool g_stage_events_on = false;
 
@@ -132,11 +132,11 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // register file); GEMM2 holds one accumulator and goes to 128.
   const int bn_auto = pick_bn(T, E_l);
   // Tokens-on-M GEMMs (gemm_tm.cu) from kTmMinTokens: their 128-row token
-  // tiles fill the MMA once experts see ~48+ tokens each.  Below that the
+  // tiles fill the MMA once experts see ~40+ tokens each.  Below that the
   // weights-on-M GEMMs (gemm_fp8.cu) size the MMA's N to the few tokens an
   // expert has.  Measured on B200 with 32 local experts, layer us
-  // weights-on-M / tokens-on-M: T=1024 385/424, 2048 575/502, 4096 932/666,
-  // 8192 1697/1093.
+  // weights-on-M / tokens-on-M: T=1024 387/411, 1280 448/443, 1536 487/451,
+  // 2048 575/455, 4096 932/664, 8192 1697/1108.
   P->tm = path_override == 2 || (path_override == 0 && T >= kTmMinTokens);
   if (P->tm) {
     // One token tile holds up to 128 rows of one expert (the MMA's M side); a

@@ -182,7 +182,7 @@ MOE_API const char* moe_fp8_ds_status_string(int status);
 MOE_API int moe_fp8_ds_set_tile_override(int32_t bn_gemm1, int32_t bn_gemm2);
 
 /* Tuning knob: 0 = automatic GEMM family (e4m3 GEMMs with weights on the
- * MMA's M side for T < 1536, e4m3 GEMMs with tokens on M from 1536 tokens),
+ * MMA's M side for T < 1280, e4m3 GEMMs with tokens on M from 1280 tokens),
  * 1 = always weights-on-M, 2 = always tokens-on-M.  Takes effect for the next
  * call (workspace size included). */
 MOE_API int moe_fp8_ds_set_path_override(int32_t mode);

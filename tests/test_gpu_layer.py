@@ -24,7 +24,7 @@ from conftest import cached_inputs, load_golden
 pytestmark = pytest.mark.gpu
 
 ATOL, RTOL = 1e-2, 2e-2
-TM_MIN_TOKENS = 1536         # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
+TM_MIN_TOKENS = 1280         # the library's automatic switch to the tokens-on-M GEMMs (api.cu)
 
 
 def _mods():
@@ -164,7 +164,7 @@ STAGE_CASES = [
     (300, 8, 0, 16, 0.0, (0, 0, 2)),       # tokens-on-M GEMMs forced at a small batch (ragged tiles)
     (64, 32, 0, 13, 0.0, (0, 0, 2)),       # tokens-on-M GEMMs, a few rows per expert, many stream-K splits
     (4200, 8, 0, 17, 0.0, (0, 0, 1)),      # weights-on-M GEMMs forced, 64/128-token tiles, many rows
-    (4200, 8, 0, 17, 0.0, (0, 0)),         # tokens-on-M GEMMs by default from 1536 tokens
+    (4200, 8, 0, 17, 0.0, (0, 0)),         # tokens-on-M GEMMs by default from 1280 tokens
     (4200, 8, 0, 17, 0.0, (48, 0, 2)),     # tokens-on-M GEMMs with 48-row tiles
     (2100, 8, 0, 18, 3.0, (0, 0)),         # tokens-on-M GEMMs, skewed routing: hot experts with many tiles
     (2100, 8, 0, 18, 3.0, (0, 0, 1)),      # weights-on-M GEMMs, skewed routing
