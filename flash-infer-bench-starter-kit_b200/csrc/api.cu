@@ -92,14 +92,19 @@ void* current_cu_context() {
 
 namespace {
 
-// Token-tile width per GEMM from the expected tokens per active expert.
-int pick_bn(int T, int E_l) {
+// Token-tile widths of the weights-on-M GEMM1 and GEMM2 from the expected
+// tokens per active expert (T*8/256).  Measured on B200 with 32 local experts
+// (layer us, GEMM1/GEMM2 widths): T=64 16/16 155 vs 16/32 159; T=128 191 vs
+// 184; T=384 277 vs 269; T=512 32/32 297 vs 16/32 305 and 64/64 328; T=640
+// 64/64 324 vs 32/32 334; T=768 353 vs 367; T=1024 64/64 387 vs 32/32 422.
+void pick_bn(int T, int E_l, int* bn1, int* bn2) {
   const double per_expert = (double)T * kTopK / kExpertsGlobal;
   (void)E_l;
-  if (per_expert <= 12.0) return 16;
-  if (per_expert <= 24.0) return 32;
-  if (per_expert <= 48.0) return 64;
-  return 128;
+  if (per_expert <= 2.0) { *bn1 = 16; *bn2 = 16; }
+  else if (per_expert <= 12.0) { *bn1 = 16; *bn2 = 32; }
+  else if (per_expert <= 16.0) { *bn1 = 32; *bn2 = 32; }
+  else if (per_expert <= 48.0) { *bn1 = 64; *bn2 = 64; }
+  else { *bn1 = 64; *bn2 = 128; }
 }
 
 struct Plan {
@@ -130,7 +135,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   // GEMM1 keeps X1 and X2 accumulators of 128 features per token column in
   // registers, so its widest tile is 64 tokens (128 would need the whole
   // register file); GEMM2 holds one accumulator and goes to 128.
-  const int bn_auto = pick_bn(T, E_l);
+  int bn_auto1 = 16, bn_auto2 = 16;
+  pick_bn(T, E_l, &bn_auto1, &bn_auto2);
   // Tokens-on-M GEMMs (gemm_tm.cu) from kTmMinTokens: their 128-row token
   // tiles fill the MMA once experts see ~40+ tokens each.  Below that the
   // weights-on-M GEMMs (gemm_fp8.cu) size the MMA's N to the few tokens an
@@ -146,8 +152,8 @@ void make_plan(int T, int E_l, int sm_count, Plan* P) {
   } else {
     // e4m3 kernels are compiled for 16, 32, 64 and 128 tokens only.
     auto compiled = [](int v) { return v == 16 || v == 32 || v == 64 || v == 128; };
-    P->bn1 = compiled(bn_override[0]) ? bn_override[0] : (bn_auto > 64 ? 64 : bn_auto);
-    P->bn2 = compiled(bn_override[1]) ? bn_override[1] : bn_auto;
+    P->bn1 = compiled(bn_override[0]) ? bn_override[0] : bn_auto1;
+    P->bn2 = compiled(bn_override[1]) ? bn_override[1] : bn_auto2;
   }
 
   auto max_mt = [&](int bn) {
